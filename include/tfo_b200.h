@@ -1,0 +1,136 @@
+/*
+ * tfo_b200.h — C ABI of the B200 (sm_100a) fused transformer-op library.
+ *
+ * Every entry point takes raw device pointers, element counts and dtype
+ * codes (no framework types), launches on the given CUDA stream (NULL = the
+ * legacy default stream), never synchronises the host, and returns a status
+ * code. On a non-zero status, tfo_last_error() returns a message for the
+ * calling thread. Inputs are read-only; outputs are caller-allocated.
+ *
+ * Each function names the reference interface it replaces
+ * (LessUp/triton-fused-ops, paths inside that project).
+ */
+#ifndef TFO_B200_H
+#define TFO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define TFO_API __attribute__((visibility("default")))
+#else
+#define TFO_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* dtype codes */
+#define TFO_DTYPE_F16 0
+#define TFO_DTYPE_BF16 1
+#define TFO_DTYPE_F32 2
+#define TFO_DTYPE_U8 3   /* reference 8-bit codec: u = int8(q) + 128 */
+#define TFO_DTYPE_E4M3 4 /* float8 e4m3fn bytes */
+
+/* status codes */
+#define TFO_OK 0
+#define TFO_ERR_INVALID 1 /* bad pointer, size or shape */
+#define TFO_ERR_DTYPE 2   /* unsupported dtype combination */
+#define TFO_ERR_CUDA 3    /* CUDA runtime error (message has the details) */
+#define TFO_ERR_DEVICE 4  /* a kernel recorded a device-side error */
+
+/* gated-MLP activations */
+#define TFO_ACT_SILU 0      /* x * sigmoid(x) */
+#define TFO_ACT_GELU 1      /* erf form: 0.5 x (1 + erf(x / sqrt 2)) */
+#define TFO_ACT_GELU_TANH 2 /* tanh approximation */
+
+/* layout of the B operand of tfo_fp8_gemm */
+#define TFO_B_KN 0 /* b is [K, N] row-major (reference fp8_gemm convention) */
+#define TFO_B_NK 1 /* b is [N, K] row-major (nn.Linear weight convention) */
+
+/* Library version string. */
+TFO_API const char* tfo_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+TFO_API const char* tfo_last_error(void);
+
+/* Synchronises the current device, then reads (and if `clear`, resets) the
+ * device error word that kernels set when a bounded wait expires. */
+TFO_API int tfo_device_error_flags(uint32_t* flags, int clear);
+
+/* Launches a one-thread kernel that waits on a barrier nothing will complete,
+ * giving up after budget_cycles SM cycles (<= 2^32) and setting the
+ * wait-timeout bit of the device error word, exactly as a GEMM pipeline wait
+ * would. Lets tests exercise the failure path without hanging a GPU.
+ * No counterpart in the reference (its kernels have no device-side waits). */
+TFO_API int tfo_selftest_bounded_wait(int64_t budget_cycles, void* stream);
+
+/* Fused RMSNorm + rotate-half RoPE over x [batch, seq_len, hidden] (contiguous).
+ * weight [hidden]; cos/sin indexed as cos[pos * cs_stride_seq + i * cs_stride_dim]
+ * for pos < seq_len, i < head_dim / 2. Columns >= num_heads * head_dim are
+ * normalised but not rotated. out has x's shape and dtype.
+ * Replaces: triton_ops/kernels/rmsnorm_rope.py:238-302 (fused_rmsnorm_rope)
+ * and its kernel :138-235. */
+TFO_API int tfo_rmsnorm_rope(const void* x, const void* weight, const void* cos, const void* sin, void* out, int64_t batch,
+                     int64_t seq_len, int64_t hidden, int64_t head_dim, int64_t num_heads, int64_t cs_stride_seq,
+                     int64_t cs_stride_dim, double eps, int x_dtype, int w_dtype, int cos_dtype, int sin_dtype,
+                     void* stream);
+
+/* Bytes of workspace needed by the dynamic-scale codec calls for numel elements. */
+TFO_API size_t tfo_fp8_scale_workspace_bytes(int64_t numel);
+
+/* Per-tensor dynamic scale: scale = fp32(448 / double(max|x|)), 1 if max|x| == 0.
+ * Writes one fp32 to scale_out (device). No host synchronisation.
+ * Replaces: triton_ops/models.py:282-299 (FP8Format.compute_scale). */
+TFO_API int tfo_fp8_compute_scale(const void* x, int64_t numel, int x_dtype, float* scale_out, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* Quantize numel elements of x (f16/bf16/f32) to out_dtype TFO_DTYPE_U8 (the
+ * reference codec, bit-exact) or TFO_DTYPE_E4M3. If `scale` is non-NULL it is
+ * used; otherwise the dynamic scale is computed on the device (needs
+ * `workspace`) and written to scale_out.
+ * Replaces: triton_ops/kernels/fp8_quantize.py:128-173 (quantize_fp8) and
+ * :21-59 (quantize_fp8_kernel). */
+TFO_API int tfo_fp8_quantize(const void* x, int64_t numel, int x_dtype, const float* scale, float* scale_out, void* out,
+                     int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Dequantize numel codes (TFO_DTYPE_U8 reference codec or TFO_DTYPE_E4M3) to
+ * out_dtype: out = dec(q) / scale.
+ * Replaces: triton_ops/kernels/fp8_quantize.py:176-211 (dequantize_fp8) and
+ * :62-98 (dequantize_fp8_kernel). */
+TFO_API int tfo_fp8_dequantize(const void* q, int64_t numel, int q_dtype, const float* scale, void* out, int out_dtype,
+                       void* stream);
+
+/* Workspace bytes tfo_fp8_gemm needs for these sizes (an upper bound over
+ * operand alignments; 0 when the product is empty). */
+TFO_API size_t tfo_fp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int ab_dtype, int b_layout);
+
+/* C[M, N] = dec(a)[M, K] . dec(b)[K, N] / (a_scale * b_scale) on tcgen05.
+ * a: [M, K] row-major codes; b: [K, N] (TFO_B_KN) or [N, K] (TFO_B_NK) codes;
+ * both TFO_DTYPE_U8 (reference codec, exact int8 products, int32 accumulation)
+ * or both TFO_DTYPE_E4M3 (fp32 accumulation). a_scale / b_scale: one fp32 each
+ * on the device. out_dtype: f16 / bf16 / f32. K <= 131072.
+ * Replaces: triton_ops/kernels/fp8_gemm.py:123-187 (fp8_gemm) and its kernel
+ * :21-120; TFO_B_NK serves FP8Linear (:272-310) without the per-call transpose. */
+TFO_API int tfo_fp8_gemm(const void* a, const void* b, const float* a_scale, const float* b_scale, void* c, int64_t M,
+                         int64_t N, int64_t K, int ab_dtype, int b_layout, int out_dtype, void* workspace,
+                         size_t workspace_bytes, void* stream);
+
+/* Workspace bytes tfo_gated_mlp needs (non-zero only when an fp32 copy of an
+ * operand is required, i.e. mixed or fp32 dtypes). */
+TFO_API size_t tfo_gated_mlp_workspace_bytes(int64_t M, int64_t N, int64_t K, int x_dtype, int w_dtype);
+
+/* out[M, N] = (x . w_gate^T) * act(x . w_up^T), x [M, K], w_gate / w_up [N, K],
+ * all row-major; fp32 accumulation; out has x's dtype. activation: TFO_ACT_*.
+ * Replaces: triton_ops/kernels/gated_mlp.py:149-218 (fused_gated_mlp) and its
+ * kernel :31-146. */
+TFO_API int tfo_gated_mlp(const void* x, const void* w_gate, const void* w_up, void* out, int64_t M, int64_t N,
+                          int64_t K, int x_dtype, int w_dtype, int activation, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* TFO_B200_H */

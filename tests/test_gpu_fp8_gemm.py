@@ -1,0 +1,164 @@
+"""FP8 GEMM on tcgen05 against the oracle and the reference's golden outputs.
+
+Tolerance (north star): relative Frobenius error <= 1e-2 against an fp32
+reference on the same quantized operands. The int8 path accumulates exactly,
+so it is also checked far tighter (<= 1e-5 in fp32 output) and bit-exactly
+on integer-valued problems.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import host, load_golden
+from oracle import tfo_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+def codes(M, K, seed, dtype=torch.float16):
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=g).to(dtype)
+    from triton_ops import quantize_fp8
+
+    return quantize_fp8(x.cuda())
+
+
+@pytest.mark.parametrize("case", sorted(load_golden("fp8_gemm")))
+def test_golden_cases(cuda, case):
+    from triton_ops import fp8_gemm
+
+    c = load_golden("fp8_gemm")[case]
+    qa = torch.from_numpy(c["qa"]).cuda()
+    qb = torch.from_numpy(c["qb"]).cuda()
+    sa = torch.tensor(float(c["sa"]), device="cuda")
+    sb = torch.tensor(float(c["sb"]), device="cuda")
+    out32 = host(fp8_gemm(qa, qb, sa, sb, torch.float32))
+    assert O.rel_fro(out32, c["c32"]) <= 1e-5
+    out16 = host(fp8_gemm(qa, qb, sa, sb))
+    assert O.rel_fro(out16, np.asarray(c["c16"], np.float32)) <= 1e-3
+
+
+def test_integer_exactness(cuda):
+    """With sa = sb = 448/127 the output is sum_k (ua-128)(ub-128) exactly (|sum| < 2^24)."""
+    from triton_ops import fp8_gemm
+
+    rng = np.random.default_rng(1)
+    for M, N, K in [(128, 256, 512), (200, 136, 1000), (7, 300, 64), (256, 512, 4096)]:
+        ua = rng.integers(1, 256, (M, K), dtype=np.uint8)
+        ub = rng.integers(1, 256, (K, N), dtype=np.uint8)
+        s = torch.tensor(448.0 / 127.0, device="cuda")
+        out = host(fp8_gemm(torch.from_numpy(ua).cuda(), torch.from_numpy(ub).cuda(), s, s, torch.float32))
+        exact = (ua.astype(np.int64) - 128) @ (ub.astype(np.int64) - 128)
+        assert np.abs(exact).max() < 2**24
+        # alpha = fp32((448/127)^2 / fp32(448/127)^2) may differ from 1 by an ulp
+        np.testing.assert_allclose(out, exact.astype(np.float64), rtol=2e-7, atol=0)
+
+
+@pytest.mark.parametrize("M", [16, 128, 1024])
+def test_config3_shapes(cuda, M):
+    from triton_ops import fp8_gemm
+
+    N = K = 4096
+    qa, sa = codes(M, K, 10 + M)
+    qb, sb = codes(K, N, 20)
+    out = host(fp8_gemm(qa, qb, sa, sb, torch.float32))
+    ref = O.fp8_gemm(qa.cpu().numpy(), qb.cpu().numpy(), sa.item(), sb.item(), "f32")
+    assert O.rel_fro(out, ref) <= 1e-5
+    out16 = host(fp8_gemm(qa, qb, sa, sb))
+    assert O.rel_fro(out16, O.round_to(ref, "f16")) <= TOL
+
+
+@pytest.mark.parametrize("M", [4096, 8192])
+def test_config3_large_m_sampled_rows(cuda, M):
+    from triton_ops import fp8_gemm
+
+    N = K = 4096
+    qa, sa = codes(M, K, 30 + M)
+    qb, sb = codes(K, N, 20)
+    out = fp8_gemm(qa, qb, sa, sb, torch.float32)
+    rows = torch.randperm(M, generator=torch.Generator().manual_seed(M))[:64]
+    ref = O.fp8_gemm(qa[rows.cuda()].cpu().numpy(), qb.cpu().numpy(), sa.item(), sb.item(), "f32")
+    assert O.rel_fro(host(out[rows.cuda()]), ref) <= 1e-5
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1, 1), (3, 5, 7), (33, 47, 129), (130, 260, 48), (257, 129, 272),
+                                   (64, 1000, 2048), (500, 64, 100)])
+@pytest.mark.parametrize("out_dtype", [torch.float16, torch.bfloat16, torch.float32])
+def test_ragged_shapes(cuda, M, N, K, out_dtype):
+    from triton_ops import fp8_gemm
+
+    qa, sa = codes(M, K, M + 1)
+    qb, sb = codes(K, N, N + 2)
+    out = fp8_gemm(qa, qb, sa, sb, out_dtype)
+    assert out.dtype == out_dtype and out.shape == (M, N)
+    ref = O.fp8_gemm(qa.cpu().numpy(), qb.cpu().numpy(), sa.item(), sb.item(), "f32")
+    assert O.rel_fro(host(out), ref) <= (1e-5 if out_dtype == torch.float32 else TOL)
+
+
+def test_float_inputs_quantize_like_reference(cuda):
+    from triton_ops import fp8_gemm, quantize_fp8
+
+    a = torch.randn(96, 320, device="cuda", dtype=torch.float16) * 0.1
+    b = torch.randn(320, 160, device="cuda", dtype=torch.float16) * 0.1
+    qa, sa = quantize_fp8(a)
+    qb, sb = quantize_fp8(b)
+    assert torch.equal(fp8_gemm(a, b), fp8_gemm(qa, qb, sa, sb))
+
+
+def test_e4m3_operands(cuda):
+    from triton_ops import fp8_gemm, quantize_fp8
+
+    for M, N, K in [(128, 256, 512), (77, 130, 96), (1024, 4096, 4096)]:
+        a = torch.randn(M, K, device="cuda", dtype=torch.float16)
+        b = torch.randn(K, N, device="cuda", dtype=torch.float16)
+        qa, sa = quantize_fp8(a, dtype=torch.float8_e4m3fn)
+        qb, sb = quantize_fp8(b, dtype=torch.float8_e4m3fn)
+        out = host(fp8_gemm(qa, qb, sa, sb, torch.float32))
+        ref = O.fp8_gemm_e4m3(qa.view(torch.uint8).cpu().numpy(), qb.view(torch.uint8).cpu().numpy(),
+                              sa.item(), sb.item(), "f32")
+        assert O.rel_fro(out, ref) <= 1e-5
+        # and against unquantized fp32 the e4m3 error stays at the format's level
+        assert O.rel_fro(out, host(a.float() @ b.float())) <= 0.08
+
+
+def test_fp8linear_matches_explicit_gemm(cuda):
+    from triton_ops import FP8Linear, fp8_gemm, quantize_fp8
+
+    torch.manual_seed(0)
+    lin = FP8Linear(256, 512, bias=True).cuda()
+    x = torch.randn(2, 16, 256, device="cuda", dtype=torch.float16)
+    y = lin(x)
+    assert y.shape == (2, 16, 512)
+    qx, sx = quantize_fp8(x.view(-1, 256))
+    ref = fp8_gemm(qx, lin.weight_fp8.t().contiguous(), sx, lin.weight_scale) + lin.bias
+    assert torch.equal(y.view(-1, 512), ref)
+    assert lin.weight_fp8.shape == (512, 256) and lin.weight_fp8.dtype == torch.uint8
+
+
+def test_reference_accuracy_vs_fp16(cuda):
+    """The reference's accuracy property: mean relative error vs fp16 matmul below 5%."""
+    from triton_ops import fp8_gemm
+
+    for M, N, K in [(64, 64, 64), (300, 200, 500), (512, 512, 512)]:
+        a = torch.randn(M, K, device="cuda", dtype=torch.float16) * 0.02
+        b = torch.randn(K, N, device="cuda", dtype=torch.float16) * 0.02
+        ref = torch.matmul(a, b).float()
+        out = fp8_gemm(a, b).float()
+        assert ((out - ref).abs() / (ref.abs() + 1e-6)).mean().item() < 0.05
+
+
+def test_validation(cuda):
+    from triton_ops import fp8_gemm
+    from triton_ops.exceptions import ShapeMismatchError, UnsupportedDtypeError
+
+    a = torch.zeros(8, 16, dtype=torch.uint8, device="cuda")
+    s = torch.tensor(1.0, device="cuda")
+    with pytest.raises(ShapeMismatchError):
+        fp8_gemm(a, torch.zeros(8, 8, dtype=torch.uint8, device="cuda"), s, s)
+    with pytest.raises(UnsupportedDtypeError):
+        fp8_gemm(a, torch.zeros(16, 8, dtype=torch.uint8, device="cuda"), s, s, torch.int32)
+    with pytest.raises(UnsupportedDtypeError):
+        fp8_gemm(a, torch.zeros(16, 8, dtype=torch.float8_e4m3fn, device="cuda"), s, s)

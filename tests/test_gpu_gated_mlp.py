@@ -1,0 +1,119 @@
+"""Fused gated MLP on tcgen05 against the oracle and the reference's golden outputs.
+
+Tolerance (north star): relative Frobenius error <= 1e-2 against an fp32
+reference; the reference's own element-wise test bar (rtol 1e-2, atol 1e-4)
+is applied to the golden cases as well.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import NAME_DT, dev_tensor, host, load_golden
+from oracle import tfo_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+
+
+@pytest.mark.parametrize("case", sorted(load_golden("gated_mlp")))
+def test_golden_cases(cuda, case):
+    from triton_ops import fused_gated_mlp
+
+    c = load_golden("gated_mlp")[case]
+    xd, wd = NAME_DT[str(c["x_dtype"])], NAME_DT[str(c["w_dtype"])]
+    out = fused_gated_mlp(dev_tensor(c["x"], xd), dev_tensor(c["wg"], wd), dev_tensor(c["wu"], wd), str(c["act"]))
+    ref = np.asarray(c["out"], np.float32)
+    got = host(out)
+    assert O.rel_fro(got, ref) <= TOL
+    np.testing.assert_allclose(got, ref, rtol=1e-2, atol=2e-3 if wd == "f32" and xd != "f32" else 1e-3)
+
+
+def mlp_inputs(M, N, K, xd="f16", wd="f16", wstd=0.02, seed=0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(M, K, device="cuda", generator=g).to(getattr(torch, {"f16": "float16", "bf16": "bfloat16", "f32": "float32"}[xd]))
+    wdt = getattr(torch, {"f16": "float16", "bf16": "bfloat16", "f32": "float32"}[wd])
+    wg = (torch.randn(N, K, device="cuda", generator=g) * wstd).to(wdt)
+    wu = (torch.randn(N, K, device="cuda", generator=g) * wstd).to(wdt)
+    return x, wg, wu
+
+
+@pytest.mark.parametrize("act", ["silu", "gelu", "gelu_tanh"])
+def test_config4_shape_sampled_rows(cuda, act):
+    """x [2, 1024, 4096], W [11264, 4096]: 128 sampled rows against the float64 oracle."""
+    from triton_ops import fused_gated_mlp
+
+    B, S, K, N = 2, 1024, 4096, 11264
+    x, wg, wu = mlp_inputs(B * S, N, K, seed=4)
+    out = fused_gated_mlp(x.view(B, S, K), wg, wu, act).view(B * S, N)
+    rows = torch.randperm(B * S, generator=torch.Generator().manual_seed(1))[:128].cuda()
+    ref = O.gated_mlp(host(x[rows]), host(wg), host(wu), act, "f16")
+    got = host(out[rows])
+    assert O.rel_fro(got, ref) <= 2e-3
+    assert np.isfinite(got).all()
+
+
+@pytest.mark.parametrize("M,N,K,xd,wd,act", [
+    (1, 128, 64, "f16", "f16", "silu"),
+    (100, 200, 136, "f16", "f16", "gelu"),
+    (129, 257, 512, "bf16", "bf16", "silu"),
+    (256, 384, 1024, "bf16", "bf16", "gelu_tanh"),
+    (64, 96, 256, "f16", "f32", "silu"),      # module case: fp32 weights -> tf32 path
+    (50, 70, 96, "f32", "f32", "gelu"),       # tf32 path
+    (33, 65, 100, "f16", "f16", "silu"),      # K % 8 != 0: CUDA-core path
+    (40, 50, 30, "f32", "f32", "silu"),       # K % 4 != 0: CUDA-core path
+    (16, 11264, 4096, "f16", "f16", "silu"),  # decode-like M
+])
+def test_shapes_dtypes_paths(cuda, M, N, K, xd, wd, act):
+    from triton_ops import fused_gated_mlp
+
+    x, wg, wu = mlp_inputs(M, N, K, xd, wd, wstd=0.1, seed=M + N + K)
+    out = fused_gated_mlp(x.view(1, M, K), wg, wu, act)
+    assert out.dtype == x.dtype and out.shape == (1, M, N)
+    ref = O.gated_mlp(host(x), host(wg), host(wu), act, {"f16": "f16", "bf16": "bf16", "f32": "f32"}[xd])
+    tf32 = "f32" in (xd, wd) and K % 4 == 0
+    assert O.rel_fro(host(out)[0], ref) <= (TOL if tf32 else 3e-3)
+
+
+def test_weights_swapped_gives_activation_on_gate(cuda):
+    """The BASELINE form act(x Wg^T) * (x Wu^T) is the reference op with the weights swapped."""
+    from triton_ops import fused_gated_mlp
+
+    x, wg, wu = mlp_inputs(256, 512, 512, seed=9)
+    out = host(fused_gated_mlp(x.view(1, 256, 512), wu, wg, "silu"))[0]
+    xf = host(x).astype(np.float64)
+    g = xf @ host(wg).astype(np.float64).T
+    u = xf @ host(wu).astype(np.float64).T
+    ref = (O.activation(g, "silu") * u).astype(np.float32)
+    assert O.rel_fro(out, O.round_to(ref, "f16")) <= 3e-3
+
+
+def test_module_and_reference_test_bar(cuda):
+    from triton_ops import FusedGatedMLP
+    from triton_ops.kernels.gated_mlp import fused_gated_mlp, gated_mlp_reference
+
+    m = FusedGatedMLP(256, 512, activation="silu").cuda()
+    x = torch.randn(2, 16, 256, device="cuda", dtype=torch.float16)
+    y = m(x)
+    assert y.shape == (2, 16, 512) and y.dtype == torch.float16
+    for act in ("silu", "gelu"):
+        x = torch.randn(2, 32, 512, device="cuda", dtype=torch.float16)
+        wg = torch.randn(1024, 512, device="cuda", dtype=torch.float16) * 0.1
+        wu = torch.randn(1024, 512, device="cuda", dtype=torch.float16) * 0.1
+        torch.backends.cuda.matmul.allow_tf32 = False
+        ref = gated_mlp_reference(x, wg, wu, act)
+        out = fused_gated_mlp(x, wg, wu, act)
+        assert torch.allclose(out.float(), ref.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_validation(cuda):
+    from triton_ops import fused_gated_mlp
+    from triton_ops.exceptions import ShapeMismatchError
+
+    x = torch.randn(2, 16, 256, device="cuda", dtype=torch.float16)
+    w = torch.randn(512, 256, device="cuda", dtype=torch.float16)
+    with pytest.raises(ValueError):
+        fused_gated_mlp(x, w, w, "relu")
+    with pytest.raises(ShapeMismatchError):
+        fused_gated_mlp(x, w, w[:, :128].contiguous())

@@ -1,0 +1,291 @@
+// C-ABI layer: argument checks, status/error reporting, device caches and
+// dispatch into the kernel translation units.
+#include <mutex>
+#include <string>
+#include <tuple>
+#include <map>
+
+#include "capi_internal.h"
+#include "common.cuh"
+#include "tfo_b200.h"
+
+namespace tfo {
+
+__device__ uint32_t g_error_word = 0;
+
+namespace {
+thread_local std::string g_last_error;
+
+int fail(int code, const std::string& msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* where) {
+  return fail(TFO_ERR_CUDA, std::string(where) + ": " + cudaGetErrorName(e) + ": " + cudaGetErrorString(e));
+}
+
+bool is_float_dtype(int d) { return d == F16 || d == BF16 || d == F32; }
+
+std::mutex g_cache_mu;
+std::map<int, int> g_sm_count;
+std::map<std::tuple<const void*, int, size_t, int>, int> g_occ;
+}  // namespace
+
+uint32_t* error_word_ptr() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static std::map<int, uint32_t*> ptrs;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = ptrs.find(dev);
+  if (it != ptrs.end()) return it->second;
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_error_word) != cudaSuccess) p = nullptr;
+  ptrs[dev] = static_cast<uint32_t*>(p);
+  return static_cast<uint32_t*>(p);
+}
+
+int num_sms() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(g_cache_mu);
+  auto it = g_sm_count.find(dev);
+  if (it != g_sm_count.end()) return it->second;
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  g_sm_count[dev] = n;
+  return n;
+}
+
+int cached_occupancy(const void* kernel, int block, size_t smem) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const auto key = std::make_tuple(kernel, block, smem, dev);
+  {
+    std::lock_guard<std::mutex> lk(g_cache_mu);
+    auto it = g_occ.find(key);
+    if (it != g_occ.end()) return it->second;
+  }
+  int occ = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, block, smem) != cudaSuccess || occ <= 0) occ = 1;
+  std::lock_guard<std::mutex> lk(g_cache_mu);
+  g_occ[key] = occ;
+  return occ;
+}
+
+size_t scale_workspace_bytes(int64_t numel) {
+  return static_cast<size_t>(amax_partials_count(numel)) * sizeof(uint32_t);
+}
+
+// Waits on an mbarrier that nothing ever arrives on, with the given cycle
+// budget, to exercise the bounded-wait error path end to end.
+__global__ void selftest_bounded_wait_kernel(long long budget, uint32_t* err) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const long long t0 = clock64();
+    while (!mbar_try_wait(&bar, 0)) {
+      if (clock64() - t0 > budget) {
+        set_error(err, ERR_WAIT_TIMEOUT_OTHER);
+        break;
+      }
+    }
+  }
+}
+
+}  // namespace tfo
+
+using namespace tfo;
+
+extern "C" {
+
+const char* tfo_version(void) { return "tfo_b200 0.1.0 (sm_100a)"; }
+
+const char* tfo_last_error(void) { return g_last_error.c_str(); }
+
+int tfo_device_error_flags(uint32_t* flags, int clear) {
+  if (flags == nullptr) return fail(TFO_ERR_INVALID, "tfo_device_error_flags: flags is NULL");
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "tfo_device_error_flags: synchronize");
+  e = cudaMemcpyFromSymbol(flags, g_error_word, sizeof(uint32_t));
+  if (e != cudaSuccess) return cuda_fail(e, "tfo_device_error_flags: read");
+  if (clear) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_error_word, &zero, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "tfo_device_error_flags: clear");
+  }
+  return TFO_OK;
+}
+
+int tfo_rmsnorm_rope(const void* x, const void* weight, const void* cos, const void* sin, void* out, int64_t batch,
+                     int64_t seq_len, int64_t hidden, int64_t head_dim, int64_t num_heads, int64_t cs_stride_seq,
+                     int64_t cs_stride_dim, double eps, int x_dtype, int w_dtype, int cos_dtype, int sin_dtype,
+                     void* stream) {
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(w_dtype) || !is_float_dtype(cos_dtype) ||
+      !is_float_dtype(sin_dtype))
+    return fail(TFO_ERR_DTYPE, "tfo_rmsnorm_rope: dtypes must be f16, bf16 or f32");
+  if (batch < 0 || seq_len < 0 || hidden <= 0 || head_dim <= 0 || num_heads < 0)
+    return fail(TFO_ERR_INVALID, "tfo_rmsnorm_rope: negative or zero dimension");
+  if (head_dim % 2 != 0) return fail(TFO_ERR_INVALID, "tfo_rmsnorm_rope: head_dim must be even");
+  if (num_heads * head_dim > hidden)
+    return fail(TFO_ERR_INVALID, "tfo_rmsnorm_rope: num_heads * head_dim exceeds hidden");
+  if (hidden > (1 << 20) || seq_len > (1ll << 31) - 1)
+    return fail(TFO_ERR_INVALID, "tfo_rmsnorm_rope: hidden or seq_len too large");
+  if (batch == 0 || seq_len == 0) return TFO_OK;
+  if (!x || !weight || !cos || !sin || !out) return fail(TFO_ERR_INVALID, "tfo_rmsnorm_rope: NULL pointer");
+  RmsNormRopeArgs a{x,         weight,    cos,           sin,           out,       batch,
+                    seq_len,   hidden,    head_dim,      num_heads,     cs_stride_seq,
+                    cs_stride_dim, static_cast<float>(eps), x_dtype, w_dtype,  cos_dtype, sin_dtype};
+  cudaError_t e = rmsnorm_rope_launch(a, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tfo_rmsnorm_rope");
+  return TFO_OK;
+}
+
+size_t tfo_fp8_scale_workspace_bytes(int64_t numel) { return scale_workspace_bytes(numel); }
+
+int tfo_fp8_compute_scale(const void* x, int64_t numel, int x_dtype, float* scale_out, void* workspace,
+                          size_t workspace_bytes, void* stream) {
+  if (!is_float_dtype(x_dtype)) return fail(TFO_ERR_DTYPE, "tfo_fp8_compute_scale: x must be f16, bf16 or f32");
+  if (numel < 0) return fail(TFO_ERR_INVALID, "tfo_fp8_compute_scale: negative numel");
+  if (!scale_out || (numel > 0 && !x)) return fail(TFO_ERR_INVALID, "tfo_fp8_compute_scale: NULL pointer");
+  const int nparts = amax_partials_count(numel);
+  if (!workspace || workspace_bytes < static_cast<size_t>(nparts) * sizeof(uint32_t))
+    return fail(TFO_ERR_INVALID, "tfo_fp8_compute_scale: workspace too small");
+  auto st = static_cast<cudaStream_t>(stream);
+  uint32_t* parts = static_cast<uint32_t*>(workspace);
+  cudaError_t e = amax_partials_launch(x, numel, x_dtype, parts, nparts, st);
+  if (e == cudaSuccess) e = finalize_scale_launch(parts, nparts, scale_out, st);
+  if (e != cudaSuccess) return cuda_fail(e, "tfo_fp8_compute_scale");
+  return TFO_OK;
+}
+
+int tfo_fp8_quantize(const void* x, int64_t numel, int x_dtype, const float* scale, float* scale_out, void* out,
+                     int out_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!is_float_dtype(x_dtype)) return fail(TFO_ERR_DTYPE, "tfo_fp8_quantize: x must be f16, bf16 or f32");
+  if (out_dtype != U8 && out_dtype != E4M3) return fail(TFO_ERR_DTYPE, "tfo_fp8_quantize: out must be U8 or E4M3");
+  if (numel < 0) return fail(TFO_ERR_INVALID, "tfo_fp8_quantize: negative numel");
+  auto st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaSuccess;
+  if (scale == nullptr) {
+    if (!scale_out) return fail(TFO_ERR_INVALID, "tfo_fp8_quantize: dynamic scale needs scale_out");
+    const int nparts = amax_partials_count(numel);
+    if (!workspace || workspace_bytes < static_cast<size_t>(nparts) * sizeof(uint32_t))
+      return fail(TFO_ERR_INVALID, "tfo_fp8_quantize: workspace too small");
+    uint32_t* parts = static_cast<uint32_t*>(workspace);
+    if (numel == 0) {
+      e = amax_partials_launch(x, 0, x_dtype, parts, nparts, st);
+      if (e == cudaSuccess) e = finalize_scale_launch(parts, nparts, scale_out, st);
+      if (e != cudaSuccess) return cuda_fail(e, "tfo_fp8_quantize");
+      return TFO_OK;
+    }
+    if (!x || !out) return fail(TFO_ERR_INVALID, "tfo_fp8_quantize: NULL pointer");
+    e = amax_partials_launch(x, numel, x_dtype, parts, nparts, st);
+    if (e == cudaSuccess) e = encode_launch(x, numel, x_dtype, nullptr, parts, nparts, scale_out, out, out_dtype, st);
+  } else {
+    if (numel == 0) return TFO_OK;
+    if (!x || !out) return fail(TFO_ERR_INVALID, "tfo_fp8_quantize: NULL pointer");
+    e = encode_launch(x, numel, x_dtype, scale, nullptr, 0, nullptr, out, out_dtype, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "tfo_fp8_quantize");
+  return TFO_OK;
+}
+
+int tfo_fp8_dequantize(const void* q, int64_t numel, int q_dtype, const float* scale, void* out, int out_dtype,
+                       void* stream) {
+  if (q_dtype != U8 && q_dtype != E4M3) return fail(TFO_ERR_DTYPE, "tfo_fp8_dequantize: q must be U8 or E4M3");
+  if (!is_float_dtype(out_dtype)) return fail(TFO_ERR_DTYPE, "tfo_fp8_dequantize: out must be f16, bf16 or f32");
+  if (numel < 0) return fail(TFO_ERR_INVALID, "tfo_fp8_dequantize: negative numel");
+  if (numel == 0) return TFO_OK;
+  if (!q || !scale || !out) return fail(TFO_ERR_INVALID, "tfo_fp8_dequantize: NULL pointer");
+  cudaError_t e = dequantize_launch(q, numel, q_dtype, scale, out, out_dtype, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "tfo_fp8_dequantize");
+  return TFO_OK;
+}
+
+size_t tfo_fp8_gemm_workspace_bytes(int64_t M, int64_t N, int64_t K, int ab_dtype, int b_layout) {
+  Fp8GemmArgs g{};
+  g.M = M; g.N = N; g.K = K; g.ab_dtype = ab_dtype; g.b_layout = b_layout;
+  return (M <= 0 || N <= 0 || K <= 0) ? 0 : fp8_gemm_workspace_bytes(g);
+}
+
+int tfo_fp8_gemm(const void* a, const void* b, const float* a_scale, const float* b_scale, void* c, int64_t M,
+                 int64_t N, int64_t K, int ab_dtype, int b_layout, int out_dtype, void* workspace,
+                 size_t workspace_bytes, void* stream) {
+  if (ab_dtype != U8 && ab_dtype != E4M3) return fail(TFO_ERR_DTYPE, "tfo_fp8_gemm: operands must be U8 or E4M3");
+  if (!is_float_dtype(out_dtype)) return fail(TFO_ERR_DTYPE, "tfo_fp8_gemm: output must be f16, bf16 or f32");
+  if (b_layout != TFO_B_KN && b_layout != TFO_B_NK) return fail(TFO_ERR_INVALID, "tfo_fp8_gemm: bad b_layout");
+  if (M < 0 || N < 0 || K < 0) return fail(TFO_ERR_INVALID, "tfo_fp8_gemm: negative dimension");
+  if (M > INT32_MAX || N > INT32_MAX || K > 131072)
+    return fail(TFO_ERR_INVALID, "tfo_fp8_gemm: M, N must fit in int32 and K <= 131072 (exact int32 accumulation)");
+  if (M == 0 || N == 0) return TFO_OK;
+  if (!c || !a_scale || !b_scale) return fail(TFO_ERR_INVALID, "tfo_fp8_gemm: NULL pointer");
+  auto st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (K == 0) {
+    const size_t esz = out_dtype == F32 ? 4 : 2;
+    e = cudaMemsetAsync(c, 0, static_cast<size_t>(M) * N * esz, st);
+    if (e != cudaSuccess) return cuda_fail(e, "tfo_fp8_gemm");
+    return TFO_OK;
+  }
+  if (!a || !b) return fail(TFO_ERR_INVALID, "tfo_fp8_gemm: NULL operand");
+  Fp8GemmArgs g{a, b, a_scale, b_scale, c, M, N, K, ab_dtype, b_layout, out_dtype, workspace, workspace_bytes};
+  if (workspace_bytes < fp8_gemm_workspace_bytes(g) || !workspace)
+    return fail(TFO_ERR_INVALID, "tfo_fp8_gemm: workspace smaller than tfo_fp8_gemm_workspace_bytes()");
+  e = fp8_gemm_launch(g, st);
+  if (e != cudaSuccess) return cuda_fail(e, "tfo_fp8_gemm");
+  return TFO_OK;
+}
+
+size_t tfo_gated_mlp_workspace_bytes(int64_t M, int64_t N, int64_t K, int x_dtype, int w_dtype) {
+  if (M <= 0 || N <= 0 || K <= 0) return 0;
+  GatedMlpArgs g{};
+  g.M = M; g.N = N; g.K = K; g.x_dtype = x_dtype; g.w_dtype = w_dtype;
+  // alignment-independent upper bound: pretend every pointer is aligned
+  g.x = g.wg = g.wu = reinterpret_cast<const void*>(uintptr_t(256));
+  g.out = reinterpret_cast<void*>(uintptr_t(256));
+  return gated_mlp_workspace_bytes(g);
+}
+
+int tfo_gated_mlp(const void* x, const void* w_gate, const void* w_up, void* out, int64_t M, int64_t N, int64_t K,
+                  int x_dtype, int w_dtype, int activation, void* workspace, size_t workspace_bytes, void* stream) {
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(w_dtype))
+    return fail(TFO_ERR_DTYPE, "tfo_gated_mlp: dtypes must be f16, bf16 or f32");
+  if (activation < TFO_ACT_SILU || activation > TFO_ACT_GELU_TANH)
+    return fail(TFO_ERR_INVALID, "tfo_gated_mlp: unknown activation");
+  if (M < 0 || N < 0 || K < 0) return fail(TFO_ERR_INVALID, "tfo_gated_mlp: negative dimension");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(TFO_ERR_INVALID, "tfo_gated_mlp: dimensions must fit in int32");
+  if (M == 0 || N == 0) return TFO_OK;
+  if (!out) return fail(TFO_ERR_INVALID, "tfo_gated_mlp: NULL output");
+  auto st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (K == 0) {
+    const size_t esz = x_dtype == F32 ? 4 : 2;
+    e = cudaMemsetAsync(out, 0, static_cast<size_t>(M) * N * esz, st);
+    if (e != cudaSuccess) return cuda_fail(e, "tfo_gated_mlp");
+    return TFO_OK;
+  }
+  if (!x || !w_gate || !w_up) return fail(TFO_ERR_INVALID, "tfo_gated_mlp: NULL operand");
+  GatedMlpArgs g{x, w_gate, w_up, out, M, N, K, x_dtype, w_dtype, activation, workspace, workspace_bytes};
+  if (workspace_bytes < gated_mlp_workspace_bytes(g))
+    return fail(TFO_ERR_INVALID, "tfo_gated_mlp: workspace smaller than tfo_gated_mlp_workspace_bytes()");
+  e = gated_mlp_launch(g, st);
+  if (e != cudaSuccess) return cuda_fail(e, "tfo_gated_mlp");
+  return TFO_OK;
+}
+
+int tfo_selftest_bounded_wait(int64_t budget_cycles, void* stream) {
+  if (budget_cycles <= 0 || budget_cycles > (1ll << 32))
+    return fail(TFO_ERR_INVALID, "tfo_selftest_bounded_wait: budget must be in (0, 2^32] cycles");
+  selftest_bounded_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(budget_cycles, error_word_ptr());
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "tfo_selftest_bounded_wait");
+  return TFO_OK;
+}
+
+}  // extern "C"

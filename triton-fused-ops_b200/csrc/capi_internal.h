@@ -1,0 +1,74 @@
+// Internal launch interfaces between the C-ABI layer (capi.cu) and the
+// kernel translation units. Nothing here is exported.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include <algorithm>
+
+namespace tfo {
+
+// Device address of the current device's error word (cached per device).
+uint32_t* error_word_ptr();
+// Number of SMs of the current device (cached per device).
+int num_sms();
+// cudaOccupancyMaxActiveBlocksPerMultiprocessor, cached per (kernel, block, smem).
+int cached_occupancy(const void* kernel, int block, size_t smem);
+
+struct RmsNormRopeArgs {
+  const void* x;
+  const void* weight;
+  const void* cos;
+  const void* sin;
+  void* out;
+  int64_t batch, seq_len, hidden, head_dim, num_heads;
+  int64_t cs_stride_seq, cs_stride_dim;
+  float eps;
+  int x_dtype, w_dtype, cos_dtype, sin_dtype;
+};
+cudaError_t rmsnorm_rope_launch(const RmsNormRopeArgs& a, cudaStream_t st);
+
+// FP8 codec (fp8_codec.cu)
+int amax_partials_count(int64_t n);
+cudaError_t amax_partials_launch(const void* x, int64_t n, int x_dtype, uint32_t* partials, int nparts,
+                                 cudaStream_t st);
+cudaError_t finalize_scale_launch(const uint32_t* partials, int nparts, float* scale_out, cudaStream_t st);
+// Encodes x with either a given scale (scale_in) or the dynamic scale reduced
+// from `partials` (then scale_out, if non-null, receives it).
+cudaError_t encode_launch(const void* x, int64_t n, int x_dtype, const float* scale_in, const uint32_t* partials,
+                          int nparts, float* scale_out, void* out, int out_dtype, cudaStream_t st);
+cudaError_t dequantize_launch(const void* q, int64_t n, int q_dtype, const float* scale, void* out, int out_dtype,
+                              cudaStream_t st);
+
+// FP8 GEMM (fp8_gemm.cu). b_layout: 0 = [K, N] row-major, 1 = [N, K] row-major.
+struct Fp8GemmArgs {
+  const void* a;
+  const void* b;
+  const float* sa;
+  const float* sb;
+  void* c;
+  int64_t M, N, K;
+  int ab_dtype, b_layout, out_dtype;
+  void* ws;
+  size_t ws_bytes;
+};
+size_t fp8_gemm_workspace_bytes(const Fp8GemmArgs& g);
+int fp8_gemm_block_n(int64_t M, int64_t N);
+cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st);
+
+// Gated MLP (gated_mlp.cu): out[M, N] = (x Wg^T) * act(x Wu^T), x [M, K], W [N, K].
+struct GatedMlpArgs {
+  const void* x;
+  const void* wg;
+  const void* wu;
+  void* out;
+  int64_t M, N, K;
+  int x_dtype, w_dtype, act;
+  void* ws;
+  size_t ws_bytes;
+};
+size_t gated_mlp_workspace_bytes(const GatedMlpArgs& g);
+cudaError_t gated_mlp_launch(const GatedMlpArgs& g, cudaStream_t st);
+}  // namespace tfo

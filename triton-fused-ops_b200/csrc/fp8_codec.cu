@@ -1,0 +1,392 @@
+// FP8 codec kernels: per-tensor amax -> scale, encode, decode.
+//
+// Two 8-bit encodings are produced from the same scaled value c = fp32(x)*s:
+//  * the reference codec ("uint8"), bit-exact with
+//    triton_ops/kernels/fp8_quantize.py:258-287:
+//        u = uint8( int8( rint( RN(RN(clamp(c, +-448) / 448) * 127) ) ) + 128 )
+//  * true e4m3fn bytes: RN_e4m3( clamp(c, +-448) ), saturating, NaN kept.
+// The dynamic scale follows triton_ops/models.py:282-299: amax = max|x| (in
+// x's dtype), scale = fp32(448.0 / double(amax)), or 1.0 when amax == 0.
+//
+// Pipeline for a dynamic scale (no host sync, no zero-initialised memory):
+//   amax_partial_kernel : grid-stride max|x|, one partial per CTA
+//   encode kernel       : every CTA reduces the partials (a few KB from L2),
+//                         derives the scale in double, CTA 0 publishes it,
+//                         then encodes its share of the tensor.
+// The second read of x is served by L2 for tensors that fit in it.
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace tfo {
+
+// Exact thresholds of the reference codec in |c|: code k >= 1 is produced iff
+// |c| >= g_q_thresh[k]; g_q_thresh[0] = 0, g_q_thresh[128] = +inf.
+__device__ float g_q_thresh[129];
+
+// The reference codec magnitude for c >= 0 (the code is odd-symmetric).
+__device__ __forceinline__ int ref_code_exact(float c) {
+  const float t = __fmul_rn(__fdiv_rn(c, 448.0f), 127.0f);
+  return static_cast<int>(rintf(t));
+}
+
+// One thread per code: binary search for the smallest fp32 value producing it.
+__global__ void init_thresholds_kernel() {
+  const int k = threadIdx.x;
+  if (k > 128) return;
+  if (k == 0) { g_q_thresh[0] = 0.f; return; }
+  if (k == 128) { g_q_thresh[128] = __int_as_float(0x7f800000); return; }
+  uint32_t lo = 0, hi = __float_as_uint(448.0f);  // f(lo) < k <= f(hi)
+  while (hi - lo > 1) {
+    const uint32_t mid = lo + (hi - lo) / 2;
+    if (ref_code_exact(__uint_as_float(mid)) >= k) hi = mid; else lo = mid;
+  }
+  g_q_thresh[k] = __uint_as_float(hi);
+}
+
+__device__ __forceinline__ float min_nan(float a, float b) {
+  float r;
+  asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ float max_nan(float a, float b) {
+  float r;
+  asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+// Reference-codec byte for scaled value c, using the threshold table in smem.
+// k0 = floor(|c|*127/448 + 0.5 - 2^-12) is k or k-1 (the margin dominates the
+// fp32 error of the estimate and sends exact .5 ties low), so one comparison
+// with the exact threshold finishes the job. NaN gives code 0 (byte 128), as
+// the reference's float->int8 conversion does.
+__device__ __forceinline__ uint32_t ref_encode(float c, const float* __restrict__ th) {
+  const float a = min_nan(fabsf(c), 448.0f);
+  const float u = __fmaf_rn(a, 0.28348214285714285f, 0.5f - 0.000244140625f);
+  int k = __float2int_rz(u);  // NaN -> 0
+  k += (a >= th[k + 1]) ? 1 : 0;
+  const int code = (c < 0.f) ? -k : k;
+  return static_cast<uint32_t>(code + 128) & 0xffu;
+}
+
+// ---- loading 16 elements as fp32 ------------------------------------------
+template <typename T> struct Load16;
+template <> struct Load16<__half> {
+  static constexpr int VECS = 2;  // 16-byte vectors per 16 elements
+  template <bool STREAM>
+  __device__ static void go(const __half* p, float (&f)[16]) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      uint4 u = STREAM ? __ldcs(q + v) : __ldg(q + v);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 p2 = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+        f[v * 8 + 2 * i] = p2.x;
+        f[v * 8 + 2 * i + 1] = p2.y;
+      }
+    }
+  }
+};
+template <> struct Load16<__nv_bfloat16> {
+  static constexpr int VECS = 2;
+  template <bool STREAM>
+  __device__ static void go(const __nv_bfloat16* p, float (&f)[16]) {
+    const uint4* q = reinterpret_cast<const uint4*>(p);
+#pragma unroll
+    for (int v = 0; v < 2; ++v) {
+      uint4 u = STREAM ? __ldcs(q + v) : __ldg(q + v);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float2 p2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
+        f[v * 8 + 2 * i] = p2.x;
+        f[v * 8 + 2 * i + 1] = p2.y;
+      }
+    }
+  }
+};
+template <> struct Load16<float> {
+  static constexpr int VECS = 4;
+  template <bool STREAM>
+  __device__ static void go(const float* p, float (&f)[16]) {
+    const float4* q = reinterpret_cast<const float4*>(p);
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      float4 u = STREAM ? __ldcs(q + v) : __ldg(q + v);
+      f[4 * v] = u.x; f[4 * v + 1] = u.y; f[4 * v + 2] = u.z; f[4 * v + 3] = u.w;
+    }
+  }
+};
+
+// ---- amax ------------------------------------------------------------------
+constexpr int kAmaxThreads = 256;
+
+template <typename T>
+__global__ void __launch_bounds__(kAmaxThreads) amax_partial_kernel(const T* __restrict__ x, int64_t n, bool vec,
+                                                                     uint32_t* __restrict__ partials) {
+  uint32_t m = 0;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if (vec) {
+    const int64_t n16 = n / 16;
+    for (int64_t i = tid; i < n16; i += stride) {
+      float f[16];
+      Load16<T>::template go<false>(x + i * 16, f);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) m = max(m, __float_as_uint(fabsf(f[j])));
+    }
+    done = n16 * 16;
+  }
+  for (int64_t i = done + tid; i < n; i += stride) m = max(m, __float_as_uint(fabsf(Ty<T>::to_f(x[i]))));
+  m = warp_max_u32(m);
+  __shared__ uint32_t red[kAmaxThreads / 32];
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t b = 0;
+    for (int i = 0; i < kAmaxThreads / 32; ++i) b = max(b, red[i]);
+    partials[blockIdx.x] = b;
+  }
+}
+
+// Reduce the per-CTA partial maxima and derive the scale exactly as the
+// reference's host code does (double division, then rounding to fp32).
+__device__ __forceinline__ float reduce_partials_to_scale(const uint32_t* __restrict__ partials, int nparts,
+                                                          uint32_t* red /* smem, >= blockDim/32 */) {
+  uint32_t m = 0;
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) m = max(m, partials[i]);
+  m = warp_max_u32(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  uint32_t b = 0;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) b = max(b, red[i]);
+  const float amax = __uint_as_float(b);
+  return (amax == 0.f) ? 1.0f : __double2float_rn(__ddiv_rn(448.0, static_cast<double>(amax)));
+}
+
+__global__ void finalize_scale_kernel(const uint32_t* __restrict__ partials, int nparts, float* __restrict__ scale_out) {
+  __shared__ uint32_t red[32];
+  const float s = reduce_partials_to_scale(partials, nparts, red);
+  if (threadIdx.x == 0) *scale_out = s;
+}
+
+// ---- encode ----------------------------------------------------------------
+constexpr int kEncThreads = 256;
+
+template <typename T, bool E4M3>
+__global__ void __launch_bounds__(kEncThreads) encode_kernel(const T* __restrict__ x, int64_t n, bool vec,
+                                                             const float* __restrict__ scale_in,
+                                                             const uint32_t* __restrict__ partials, int nparts,
+                                                             float* __restrict__ scale_out, uint8_t* __restrict__ out) {
+  __shared__ float th[129];
+  __shared__ float s_sh;
+  __shared__ uint32_t red[kEncThreads / 32];
+  if (!E4M3) {
+    for (int i = threadIdx.x; i < 129; i += blockDim.x) th[i] = g_q_thresh[i];
+  }
+  if (partials != nullptr) {
+    const float s = reduce_partials_to_scale(partials, nparts, red);
+    if (threadIdx.x == 0) {
+      s_sh = s;
+      if (blockIdx.x == 0 && scale_out != nullptr) *scale_out = s;
+    }
+  } else if (threadIdx.x == 0) {
+    s_sh = *scale_in;
+  }
+  __syncthreads();
+  const float s = s_sh;
+
+  auto enc1 = [&](float xf) -> uint32_t {
+    const float c = __fmul_rn(xf, s);
+    if constexpr (E4M3) {
+      const float cl = min_nan(max_nan(c, -448.0f), 448.0f);
+      return static_cast<uint32_t>(__nv_cvt_float_to_fp8(cl, __NV_SATFINITE, __NV_E4M3));
+    } else {
+      return ref_encode(c, th);
+    }
+  };
+
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if (vec) {
+    const int64_t n16 = n / 16;
+    for (int64_t i = tid; i < n16; i += stride) {
+      float f[16];
+      Load16<T>::template go<true>(x + i * 16, f);
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        w[q] = enc1(f[4 * q]) | (enc1(f[4 * q + 1]) << 8) | (enc1(f[4 * q + 2]) << 16) | (enc1(f[4 * q + 3]) << 24);
+      }
+      __stcs(reinterpret_cast<uint4*>(out) + i, make_uint4(w[0], w[1], w[2], w[3]));
+    }
+    done = n16 * 16;
+  }
+  for (int64_t i = done + tid; i < n; i += stride) out[i] = static_cast<uint8_t>(enc1(Ty<T>::to_f(x[i])));
+}
+
+// ---- decode ----------------------------------------------------------------
+constexpr int kDecThreads = 256;
+
+// out = RN_out( dec(u) / s ), dec(u) = RN(RN(float(u - 128) / 127) * 448) for
+// the reference codec (triton_ops/kernels/fp8_quantize.py:305-312) or the
+// e4m3 value of u. Only 256 outputs exist per call, so each CTA builds them
+// in shared memory and the stream becomes a table lookup.
+template <typename TO> struct Raw { using type = uint16_t; };
+template <> struct Raw<float> { using type = uint32_t; };
+
+template <typename TO>
+__device__ __forceinline__ typename Raw<TO>::type to_raw(float v) {
+  if constexpr (sizeof(TO) == 4) {
+    return __float_as_uint(v);
+  } else {
+    TO h = Ty<TO>::from_f(v);
+    return *reinterpret_cast<uint16_t*>(&h);
+  }
+}
+
+template <typename TO, bool E4M3>
+__global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __restrict__ q, int64_t n, bool vec,
+                                                             const float* __restrict__ scale, TO* __restrict__ out) {
+  using R = typename Raw<TO>::type;
+  __shared__ R lut[256];
+  const float s = *scale;
+  for (int u = threadIdx.x; u < 256; u += blockDim.x) {
+    float v;
+    if constexpr (E4M3) {
+      __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(u), __NV_E4M3);
+      v = __half2float(__half(hr));
+    } else {
+      v = __fmul_rn(__fdiv_rn(static_cast<float>(u - 128), 127.0f), 448.0f);
+    }
+    lut[u] = to_raw<TO>(__fdiv_rn(v, s));
+  }
+  __syncthreads();
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  int64_t done = 0;
+  if (vec) {
+    const int64_t n16 = n / 16;
+    for (int64_t i = tid; i < n16; i += stride) {
+      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(q) + i);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      uint32_t o[16 * sizeof(R) / 4];
+      if constexpr (sizeof(R) == 2) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          const uint32_t b0 = (w[k >> 1] >> (16 * (k & 1))) & 0xffu;
+          const uint32_t b1 = (w[k >> 1] >> (16 * (k & 1) + 8)) & 0xffu;
+          o[k] = static_cast<uint32_t>(lut[b0]) | (static_cast<uint32_t>(lut[b1]) << 16);
+        }
+      } else {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) o[k] = lut[(w[k >> 2] >> (8 * (k & 3))) & 0xffu];
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out) + i * (16 * sizeof(R) / 16);
+#pragma unroll
+      for (int v = 0; v < static_cast<int>(16 * sizeof(R) / 16); ++v)
+        __stcs(dst + v, make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]));
+    }
+    done = n16 * 16;
+  }
+  R* orow = reinterpret_cast<R*>(out);
+  for (int64_t i = done + tid; i < n; i += stride) orow[i] = lut[q[i]];
+}
+
+// ---------------------------------------------------------------------------
+// host side
+// ---------------------------------------------------------------------------
+namespace {
+bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int g_thresh_ready[64] = {0};
+
+cudaError_t ensure_thresholds(cudaStream_t st) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 64 && __atomic_load_n(&g_thresh_ready[dev], __ATOMIC_ACQUIRE)) return cudaSuccess;
+  init_thresholds_kernel<<<1, 160, 0, st>>>();
+  e = cudaGetLastError();
+  if (e == cudaSuccess && dev < 64) __atomic_store_n(&g_thresh_ready[dev], 1, __ATOMIC_RELEASE);
+  return e;
+}
+
+int grid_for(int64_t work_items, int threads, int per_sm) {
+  const int64_t want = (work_items + threads - 1) / threads;
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(num_sms()) * per_sm)));
+}
+}  // namespace
+
+int amax_partials_count(int64_t n) { return grid_for(std::max<int64_t>(n / 16, 1), kAmaxThreads, 8); }
+
+cudaError_t amax_partials_launch(const void* x, int64_t n, int x_dtype, uint32_t* partials, int nparts,
+                                 cudaStream_t st) {
+  const bool vec = al16(x);
+  switch (x_dtype) {
+    case F16: amax_partial_kernel<__half><<<nparts, kAmaxThreads, 0, st>>>(static_cast<const __half*>(x), n, vec, partials); break;
+    case BF16: amax_partial_kernel<__nv_bfloat16><<<nparts, kAmaxThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, vec, partials); break;
+    default: amax_partial_kernel<float><<<nparts, kAmaxThreads, 0, st>>>(static_cast<const float*>(x), n, vec, partials); break;
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t finalize_scale_launch(const uint32_t* partials, int nparts, float* scale_out, cudaStream_t st) {
+  finalize_scale_kernel<<<1, 256, 0, st>>>(partials, nparts, scale_out);
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t enc_t(const void* x, int64_t n, const float* scale_in, const uint32_t* partials, int nparts,
+                         float* scale_out, void* out, int out_dtype, cudaStream_t st) {
+  const bool vec = al16(x) && al16(out);
+  const int grid = grid_for(std::max<int64_t>(n / 16, 1), kEncThreads, 8);
+  if (out_dtype == E4M3) {
+    encode_kernel<T, true><<<grid, kEncThreads, 0, st>>>(static_cast<const T*>(x), n, vec, scale_in, partials, nparts,
+                                                         scale_out, static_cast<uint8_t*>(out));
+  } else {
+    encode_kernel<T, false><<<grid, kEncThreads, 0, st>>>(static_cast<const T*>(x), n, vec, scale_in, partials, nparts,
+                                                          scale_out, static_cast<uint8_t*>(out));
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t encode_launch(const void* x, int64_t n, int x_dtype, const float* scale_in, const uint32_t* partials,
+                          int nparts, float* scale_out, void* out, int out_dtype, cudaStream_t st) {
+  if (out_dtype != E4M3) {
+    cudaError_t e = ensure_thresholds(st);
+    if (e != cudaSuccess) return e;
+  }
+  switch (x_dtype) {
+    case F16: return enc_t<__half>(x, n, scale_in, partials, nparts, scale_out, out, out_dtype, st);
+    case BF16: return enc_t<__nv_bfloat16>(x, n, scale_in, partials, nparts, scale_out, out, out_dtype, st);
+    default: return enc_t<float>(x, n, scale_in, partials, nparts, scale_out, out, out_dtype, st);
+  }
+}
+
+template <typename TO>
+static cudaError_t dec_t(const void* q, int64_t n, bool e4m3, const float* scale, void* out, cudaStream_t st) {
+  const bool vec = al16(q) && al16(out);
+  const int grid = grid_for(std::max<int64_t>(n / 16, 1), kDecThreads, 8);
+  if (e4m3) {
+    decode_kernel<TO, true><<<grid, kDecThreads, 0, st>>>(static_cast<const uint8_t*>(q), n, vec, scale, static_cast<TO*>(out));
+  } else {
+    decode_kernel<TO, false><<<grid, kDecThreads, 0, st>>>(static_cast<const uint8_t*>(q), n, vec, scale, static_cast<TO*>(out));
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t dequantize_launch(const void* q, int64_t n, int q_dtype, const float* scale, void* out, int out_dtype,
+                              cudaStream_t st) {
+  const bool e4m3 = (q_dtype == E4M3);
+  switch (out_dtype) {
+    case F16: return dec_t<__half>(q, n, e4m3, scale, out, st);
+    case BF16: return dec_t<__nv_bfloat16>(q, n, e4m3, scale, out, st);
+    default: return dec_t<float>(q, n, e4m3, scale, out, st);
+  }
+}
+
+}  // namespace tfo

@@ -1,0 +1,220 @@
+// Persistent, warp-specialised tcgen05 GEMM mainloop for sm_100a.
+//
+//   D[m, n] (+)= sum_k A[m, k] * B_j[n, k]        for j < NUM_B
+//
+// A and every B_j are K-major (rows of K), staged by TMA into a STAGES-deep
+// shared-memory ring with the 128-byte swizzle; one elected thread issues
+// tcgen05.mma (M = 128, N = BLOCK_N, 32 bytes of K per instruction) into a
+// double-buffered TMEM accumulator (2 x NUM_B x BLOCK_N columns), and four
+// epilogue warps drain the finished buffer with tcgen05.ld while the next
+// tile's mainloop runs. NUM_B = 2 shares every A tile between two B operands
+// (the gate and up projections of the gated MLP).
+//
+// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer and
+// TMEM owner, warps 2-5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
+//
+// Every mbarrier wait is bounded; a wait that runs out of budget records a
+// bit in the device error word, raises a CTA-wide abort flag that the other
+// roles poll, and all roles fall through to the final barrier, where TMEM is
+// released. No TMA multicast is used.
+#pragma once
+
+#include "common.cuh"
+
+namespace tfo {
+
+template <MmaKind KIND> struct KindTraits;
+template <> struct KindTraits<MmaKind::F16> { static constexpr int ELEM = 2; };
+template <> struct KindTraits<MmaKind::TF32> { static constexpr int ELEM = 4; };
+template <> struct KindTraits<MmaKind::I8> { static constexpr int ELEM = 1; };
+template <> struct KindTraits<MmaKind::F8F6F4> { static constexpr int ELEM = 1; };
+
+struct TileSched {
+  int num_m, num_n, group_m;
+  __device__ __forceinline__ int num_tiles() const { return num_m * num_n; }
+  // Grouped raster: GROUP_M row-blocks sweep the column-blocks together so the
+  // B tiles and the A rows of a wave stay resident in L2.
+  __device__ __forceinline__ void coords(int tile, int& m_blk, int& n_blk) const {
+    const int in_group = group_m * num_n;
+    const int g = tile / in_group;
+    const int first_m = g * group_m;
+    const int gsz = min(num_m - first_m, group_m);
+    const int r = tile - g * in_group;
+    m_blk = first_m + r % gsz;
+    n_blk = r / gsz;
+  }
+};
+
+template <int BLOCK_N, int NUM_B, int STAGES>
+struct GemmLayout {
+  static constexpr int BM = 128;
+  static constexpr int A_BYTES = BM * 128;
+  static constexpr int B_BYTES = BLOCK_N * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + NUM_B * B_BYTES;
+  static constexpr int ACC_COLS = NUM_B * BLOCK_N;
+  static constexpr int TMEM_COLS = 2 * ACC_COLS;
+  static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns must be a power of two <= 512");
+  static_assert(BLOCK_N % 16 == 0 && BLOCK_N >= 16 && BLOCK_N <= 256, "UMMA N for M=128");
+  // dynamic shared memory: ring + barriers + 1 KB for manual alignment
+  static constexpr size_t SMEM_BYTES = static_cast<size_t>(STAGES) * STAGE_BYTES + 256 + 1024;
+};
+
+// Waits for `parity` on `bar`, giving up when the CTA abort flag is raised or
+// the budget runs out (then sets the error bit and raises the flag).
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* err,
+                                              uint32_t bit) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitBudgetCycles) {
+      set_error(err, bit);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// Epi must provide:
+//   struct Params;
+//   __device__ void operator()(const Params&, const uint32_t (&acc)[NUM_B][16], int row, int col0, int M, int N)
+//   called once per 16 accumulator columns per row (row < M not guaranteed).
+template <MmaKind KIND, int BLOCK_N, int NUM_B, int STAGES, class Epi>
+__global__ void __launch_bounds__(192, 1)
+    umma_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
+                     const __grid_constant__ CUtensorMap tmap_b1, int M, int N, int K, int group_m, uint32_t idesc,
+                     const typename Epi::Params ep, uint32_t* err) {
+  using L = GemmLayout<BLOCK_N, NUM_B, STAGES>;
+  constexpr int KB_ELEMS = 128 / KindTraits<KIND>::ELEM;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sa = smem;
+  uint8_t* sb = smem + STAGES * L::A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  TileSched sched{(M + L::BM - 1) / L::BM, (N + BLOCK_N - 1) / BLOCK_N, group_m};
+  const int num_tiles = sched.num_tiles();
+  const int num_k = (K + KB_ELEMS - 1) / KB_ELEMS;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b0);
+    if (NUM_B == 2) tma_prefetch_desc(&tmap_b1);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, L::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        int m_blk, n_blk;
+        sched.coords(tile, m_blk, n_blk);
+        for (int kb = 0; kb < num_k; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!wait_or_abort(&empty[s], ph ^ 1, abort_flag, err, ERR_WAIT_TIMEOUT_PRODUCER)) break;
+          mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+          const int kx = kb * KB_ELEMS;
+          tma_load_2d(sa + s * L::A_BYTES, &tmap_a, &full[s], kx, m_blk * L::BM);
+          tma_load_2d(sb + (s * NUM_B) * L::B_BYTES, &tmap_b0, &full[s], kx, n_blk * BLOCK_N);
+          if constexpr (NUM_B == 2) tma_load_2d(sb + (s * NUM_B + 1) * L::B_BYTES, &tmap_b1, &full[s], kx, n_blk * BLOCK_N);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int it = 0, tcount = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tcount) {
+        const int acc = tcount & 1;
+        const uint32_t aph = (tcount >> 1) & 1;
+        if (!wait_or_abort(&tempty[acc], aph ^ 1, abort_flag, err, ERR_WAIT_TIMEOUT_MMA)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * L::ACC_COLS;
+        bool ok = true;
+        for (int kb = 0; kb < num_k; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!wait_or_abort(&full[s], ph, abort_flag, err, ERR_WAIT_TIMEOUT_MMA)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(sa + s * L::A_BYTES);
+          const uint32_t b_addr = smem_u32(sb + (s * NUM_B) * L::B_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t adesc = smem_desc_kmajor_sw128(a_addr + kk * 32);
+#pragma unroll
+            for (int j = 0; j < NUM_B; ++j) {
+              const uint64_t bdesc = smem_desc_kmajor_sw128(b_addr + j * L::B_BYTES + kk * 32);
+              umma<KIND>(d_tmem + j * BLOCK_N, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            }
+          }
+          umma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int sub = warp & 3;
+    const int row_in_tile = sub * 32 + lane;
+    const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
+    int tcount = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tcount) {
+      const int acc = tcount & 1;
+      const uint32_t aph = (tcount >> 1) & 1;
+      if (!wait_or_abort(&tfull[acc], aph, abort_flag, err, ERR_WAIT_TIMEOUT_EPILOGUE)) break;
+      tc_fence_after();
+      int m_blk, n_blk;
+      sched.coords(tile, m_blk, n_blk);
+      const int row = m_blk * L::BM + row_in_tile;
+      const uint32_t base = tmem_base + lane_addr + acc * L::ACC_COLS;
+#pragma unroll 1
+      for (int c = 0; c < BLOCK_N; c += 16) {
+        uint32_t r[NUM_B][16];
+#pragma unroll
+        for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N + c, r[j]);
+        tmem_ld_wait();
+        Epi{}(ep, r, row, n_blk * BLOCK_N + c, M, N);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, L::TMEM_COLS);
+  }
+}
+
+}  // namespace tfo

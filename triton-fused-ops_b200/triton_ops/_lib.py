@@ -1,0 +1,158 @@
+"""ctypes binding of the sm_100a library (``_lib/libtfo_b200.so``).
+
+The library exports the C ABI declared in ``include/tfo_b200.h``. This module
+loads it on first use, declares every entry point's argument types, maps
+torch dtypes to the ABI's dtype codes, and turns non-zero status codes into
+this package's exceptions. There is no fallback: if the library is missing or
+cannot be loaded, every op raises :class:`~triton_ops.exceptions.TritonKernelError`.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+
+import torch
+
+from triton_ops.exceptions import TritonKernelError, UnsupportedDtypeError
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libtfo_b200.so"
+
+# dtype codes (include/tfo_b200.h)
+F16, BF16, F32, U8, E4M3 = 0, 1, 2, 3, 4
+_DTYPE_CODE = {
+    torch.float16: F16,
+    torch.bfloat16: BF16,
+    torch.float32: F32,
+    torch.uint8: U8,
+}
+if hasattr(torch, "float8_e4m3fn"):
+    _DTYPE_CODE[torch.float8_e4m3fn] = E4M3
+
+# status codes
+OK, ERR_INVALID, ERR_DTYPE, ERR_CUDA, ERR_DEVICE = 0, 1, 2, 3, 4
+
+# activations
+ACT_CODE = {"silu": 0, "gelu": 1, "gelu_tanh": 2}
+
+# layout of fp8_gemm's B operand
+B_KN, B_NK = 0, 1
+
+_c_i64 = ctypes.c_int64
+_c_int = ctypes.c_int
+_c_vp = ctypes.c_void_p
+_c_size = ctypes.c_size_t
+
+# name -> (restype, argtypes)
+_SIGNATURES = {
+    "tfo_version": (ctypes.c_char_p, []),
+    "tfo_last_error": (ctypes.c_char_p, []),
+    "tfo_device_error_flags": (_c_int, [ctypes.POINTER(ctypes.c_uint32), _c_int]),
+    "tfo_selftest_bounded_wait": (_c_int, [_c_i64, _c_vp]),
+    "tfo_rmsnorm_rope": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+         ctypes.c_double, _c_int, _c_int, _c_int, _c_int, _c_vp],
+    ),
+    "tfo_fp8_scale_workspace_bytes": (_c_size, [_c_i64]),
+    "tfo_fp8_compute_scale": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_size, _c_vp]),
+    "tfo_fp8_quantize": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_size, _c_vp]),
+    "tfo_fp8_dequantize": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_int, _c_vp]),
+    "tfo_fp8_gemm_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64, _c_int, _c_int]),
+    "tfo_fp8_gemm": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_vp, _c_size, _c_vp],
+    ),
+    "tfo_gated_mlp_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64, _c_int, _c_int]),
+    "tfo_gated_mlp": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_vp, _c_size, _c_vp],
+    ),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def load() -> ctypes.CDLL:
+    """Loads the library once and declares its entry points."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = Path(os.environ.get("TFO_B200_LIB", LIB_PATH))
+        if not path.exists():
+            raise TritonKernelError(
+                f"native library {path} is missing; build it with "
+                "`python triton-fused-ops_b200/build.py` (there is no fallback path)"
+            )
+        try:
+            lib = ctypes.CDLL(str(path))
+        except OSError as e:  # pragma: no cover - depends on the machine
+            raise TritonKernelError(f"cannot load native library {path}: {e}") from e
+        for name, (res, args) in _SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def declared_symbols() -> list[str]:
+    return list(_SIGNATURES)
+
+
+def dtype_code(dtype: torch.dtype, what: str = "tensor") -> int:
+    try:
+        return _DTYPE_CODE[dtype]
+    except KeyError:
+        raise UnsupportedDtypeError(
+            f"{what} has unsupported dtype {dtype}",
+            dtype=dtype,
+            supported_dtypes=list(_DTYPE_CODE),
+            tensor_name=what,
+        ) from None
+
+
+def stream_of(t: torch.Tensor) -> int:
+    """Raw handle of torch's current stream on t's device."""
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def check(status: int, what: str) -> None:
+    """Raises the package exception that matches a non-zero status code."""
+    if status == OK:
+        return
+    msg = (load().tfo_last_error() or b"").decode(errors="replace")
+    if status == ERR_DTYPE:
+        raise UnsupportedDtypeError(f"{what}: {msg}")
+    raise TritonKernelError(f"{what} failed (status {status}): {msg}")
+
+
+def call(name: str, *args) -> None:
+    """Calls entry point `name` and raises on a non-zero status."""
+    check(getattr(load(), name)(*args), name)
+
+
+def device_error_flags(clear: bool = True) -> int:
+    """Synchronises and returns (optionally clearing) the device error word."""
+    flags = ctypes.c_uint32(0)
+    check(load().tfo_device_error_flags(ctypes.byref(flags), int(clear)), "tfo_device_error_flags")
+    return int(flags.value)
+
+
+def version() -> str:
+    return load().tfo_version().decode()
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """A scratch buffer from torch's caching allocator (at least 16 bytes)."""
+    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)

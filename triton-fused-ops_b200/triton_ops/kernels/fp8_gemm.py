@@ -1,0 +1,155 @@
+"""FP8 GEMM and the FP8Linear module.
+
+``fp8_gemm(a, b, a_scale, b_scale)`` computes ``dec(a) @ dec(b) / (sa * sb)``
+on tcgen05 tensor cores (``tfo_fp8_gemm``, csrc/fp8_gemm.cu). For the
+reference's 8-bit code (``uint8`` operands) the product is an exact int8 GEMM
+with int32 accumulation; ``float8_e4m3fn`` operands use the FP8 tensor-core
+path with fp32 accumulation. Float operands are quantized first, as in the
+reference (triton_ops/kernels/fp8_gemm.py:123-187).
+
+``FP8Linear`` keeps the reference's parameters and buffers
+(fp8_gemm.py:228-310) but hands the [out, in] code matrix to the GEMM as is
+(no per-call transpose).
+
+``fp8_gemm_reference`` restates the reference's PyTorch oracle (:190-225) for
+tests; the op never calls it.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from triton_ops import _lib
+from triton_ops.exceptions import UnsupportedDtypeError
+from triton_ops.kernels._native import NativeKernel
+from triton_ops.kernels.fp8_quantize import _scale_f32, quantize_fp8
+from triton_ops.validation import SUPPORTED_DTYPES_FLOAT, validate_fp8_gemm_inputs
+
+FP8_MAX = 448.0
+
+fp8_gemm_kernel = NativeKernel(
+    "fp8_gemm_kernel", "tfo_fp8_gemm", "TMA -> smem ring -> tcgen05.mma (kind::i8 / kind::f8f6f4) -> TMEM -> epilogue"
+)
+
+_FLOATS = (torch.float16, torch.bfloat16, torch.float32)
+
+
+def _gemm_codes(a, b, a_scale, b_scale, output_dtype, b_layout):
+    """Launches tfo_fp8_gemm on code tensors; b is [K, N] (B_KN) or [N, K] (B_NK)."""
+    if a.dtype != b.dtype:
+        raise UnsupportedDtypeError(
+            f"fp8_gemm operands must share a code dtype, got {a.dtype} and {b.dtype}",
+            dtype=(a.dtype, b.dtype), supported_dtypes=[torch.uint8, getattr(torch, "float8_e4m3fn", None)],
+        )
+    code = _lib.dtype_code(a.dtype, "a")
+    if code not in (_lib.U8, _lib.E4M3):
+        raise UnsupportedDtypeError(f"fp8_gemm operands must be uint8 or float8_e4m3fn codes, got {a.dtype}",
+                                    dtype=a.dtype, tensor_name="a")
+    M, K = a.shape
+    N = b.shape[1] if b_layout == _lib.B_KN else b.shape[0]
+    c = torch.empty(M, N, dtype=output_dtype, device=a.device)
+    if c.numel() == 0:
+        return c
+    sa = _scale_f32(a_scale.to(a.device))
+    sb = _scale_f32(b_scale.to(a.device))
+    lib = _lib.load()
+    ws_bytes = lib.tfo_fp8_gemm_workspace_bytes(M, N, K, code, b_layout)
+    ws = _lib.workspace(ws_bytes, a.device)
+    _lib.call(
+        "tfo_fp8_gemm", a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), c.data_ptr(), M, N, K, code,
+        b_layout, _lib.dtype_code(output_dtype, "output_dtype"), ws.data_ptr(), ws.numel(), _lib.stream_of(a),
+    )
+    return c
+
+
+def fp8_gemm(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    a_scale: torch.Tensor = None,
+    b_scale: torch.Tensor = None,
+    output_dtype: torch.dtype = torch.float16,
+    *,
+    quant_dtype: torch.dtype = torch.uint8,
+) -> torch.Tensor:
+    """FP8 matrix product ``a @ b`` of per-tensor-scaled 8-bit operands.
+
+    Args:
+        a: [M, K] codes (``uint8`` or ``float8_e4m3fn``) or a float matrix
+        b: [K, N] codes or a float matrix
+        a_scale, b_scale: the operands' quantize multipliers (required for
+            code operands, computed for float operands)
+        output_dtype: float16 (default), bfloat16 or float32
+        quant_dtype: code dtype used when a float operand is quantized here
+            (``torch.uint8`` = the reference's code, or ``torch.float8_e4m3fn``)
+
+    Returns:
+        [M, N] tensor of `output_dtype`.
+    """
+    if a.dtype in _FLOATS:
+        a, a_scale = quantize_fp8(a, dtype=quant_dtype)
+    if b.dtype in _FLOATS:
+        b, b_scale = quantize_fp8(b, dtype=quant_dtype)
+    validate_fp8_gemm_inputs(a, b, a_scale, b_scale, output_dtype)
+    return _gemm_codes(a, b, a_scale, b_scale, output_dtype, _lib.B_KN)
+
+
+def fp8_gemm_reference(
+    a: torch.Tensor,
+    b: torch.Tensor,
+    a_scale: torch.Tensor = None,
+    b_scale: torch.Tensor = None,
+    output_dtype: torch.dtype = torch.float16,
+) -> torch.Tensor:
+    """PyTorch restatement of the reference's oracle: decode each code operand, fp32 matmul."""
+
+    def decode(t, s):
+        if t.dtype == torch.uint8:
+            return (t.to(torch.int32) - 128).float() / 127.0 * FP8_MAX / s
+        return t.float()
+
+    return torch.matmul(decode(a, a_scale), decode(b, b_scale)).to(output_dtype)
+
+
+class FP8Linear(torch.nn.Module):
+    """Linear layer whose weight is stored as per-tensor FP8 codes.
+
+    Same parameters and buffers as the reference: ``weight`` (fp32, N(0, 0.02)
+    init), optional zero ``bias``, and the ``weight_fp8`` / ``weight_scale``
+    buffers filled on the first forward (or by :meth:`quantize_weights`).
+    """
+
+    def __init__(self, in_features: int, out_features: int, bias: bool = False):
+        super().__init__()
+        self.in_features = in_features
+        self.out_features = out_features
+        self.register_buffer("weight_fp8", None)
+        self.register_buffer("weight_scale", None)
+        self.weight = torch.nn.Parameter(torch.randn(out_features, in_features) * 0.02)
+        if bias:
+            self.bias = torch.nn.Parameter(torch.zeros(out_features))
+        else:
+            self.register_parameter("bias", None)
+        self._quantized = False
+
+    def quantize_weights(self):
+        """Quantizes the weight once (reference codec, per-tensor scale)."""
+        if not self._quantized:
+            weight_fp8, weight_scale = quantize_fp8(self.weight.data)
+            self.weight_fp8 = weight_fp8
+            self.weight_scale = weight_scale
+            self._quantized = True
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        self.quantize_weights()
+        orig_shape = x.shape
+        x_2d = x.reshape(-1, self.in_features)
+        if not x_2d.is_contiguous():
+            x_2d = x_2d.contiguous()
+        x_fp8, x_scale = quantize_fp8(x_2d)
+        out_dtype = x.dtype if x.dtype in SUPPORTED_DTYPES_FLOAT else torch.float16
+        # weight_fp8 is [out, in] = [N, K]: consumed directly as the K-major B operand.
+        output = _gemm_codes(x_fp8, self.weight_fp8, x_scale, self.weight_scale, out_dtype, _lib.B_NK)
+        output = output.view(*orig_shape[:-1], self.out_features)
+        if self.bias is not None:
+            output = output + self.bias
+        return output
