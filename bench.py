@@ -1,0 +1,509 @@
+"""Benchmark of the fused transformer-op hot path on B200.
+
+Workload (one "step"): the prefill slab of a transformer layer's fused ops,
+x [8, 8192, 4096] fp16 (65,536 token rows, N(0, 1)) ->
+``fused_rmsnorm_rope`` (weight N(1, 0.1), head_dim 64, RoPE base 10000) ->
+``fused_gated_mlp`` (SiLU, gate/up weights [11264, 4096] N(0, 0.02)).
+With ``--gpus N`` the 65,536 rows are split into N contiguous slabs, one per
+rank (strong scaling); the weights are broadcast once over NCCL at setup and
+the timed step has no collective.
+
+Printed (rank 0, one JSON line): ``value`` = whole-job throughput of the step
+in TFLOP/s, counting the gated MLP's 4*M*N*K tensor flops (RMSNorm+RoPE adds
+no tensor flops but its time is inside the step); ``e2e`` = the same with
+pinned-host inputs copied in and the output copied out every step; the
+roofline of the dominant kernel (the gated MLP) and of RMSNorm+RoPE from
+CUDA events on the launching stream; per-op ``components`` (FP8 codec GB/s,
+FP8 GEMM TFLOP/s over M, RMSNorm+RoPE GB/s at the small shape) on rank 0;
+SM clocks sampled during the timed region; and the CPU baseline (the numpy
+restatement of the reference's PyTorch path, on a bounded row sample).
+
+``--impl reference`` times that CPU path alone (all host threads, bounded row
+sample per step) and prints the same metric.
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "triton-fused-ops_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "RMSNorm+RoPE HBM GB/s; FP8 GEMM & gated-MLP TFLOPS vs B200 peak"
+B, S, H, D, I = 8, 8192, 4096, 64, 11264
+ROWS = B * S
+FLOPS_PER_ROW = 4 * I * H  # gate + up projections, 2 flops per multiply-add
+RMS_BYTES_PER_ROW = 2 * H * 2  # read x + write y (fp16); weight and tables are reused across rows
+L2_BYTES = 126 * 2**20
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]), "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(prefix="clocks", suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.path is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
+            except ValueError:
+                continue
+        os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for r in rows:
+            for n, v in zip(names, r[3][1:]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        loaded = [r for r in rows if r[2] > 300] or rows
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "power_w_max": max(r[2] for r in rows), "samples": len(rows), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+def dist_setup():
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def rope_tables(seq_len: int, head_dim: int, device):
+    """HF-style cos/sin [seq_len, head_dim] = cat(f, f), f = pos * 10000^(-2i/head_dim), as fp16."""
+    import torch
+
+    inv = 1.0 / (10000.0 ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    f = torch.outer(torch.arange(seq_len, dtype=torch.float64), inv)
+    emb = torch.cat([f, f], dim=-1)
+    return emb.cos().float().half().to(device), emb.sin().float().half().to(device)
+
+
+def flush_l2(buf):
+    buf.add_(1)
+
+
+def time_events(fn, reps, flush_buf=None):
+    """Mean ms of fn() over reps, each timed alone with CUDA events (L2 flushed between reps)."""
+    import torch
+
+    st = torch.cuda.current_stream()
+    times = []
+    for _ in range(reps):
+        if flush_buf is not None:
+            flush_l2(flush_buf)
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(st)
+        fn()
+        b.record(st)
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    return sum(times) / len(times)
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: numpy restatement of the reference's PyTorch path
+# ---------------------------------------------------------------------------
+class CpuPath:
+    """The reference's CPU path restated in numpy: fp32 RMSNorm+RoPE math, fp32 gated-MLP matmuls."""
+
+    def __init__(self, sample_rows: int):
+        import numpy as np
+
+        from oracle import tfo_oracle as O
+
+        self.O = O
+        self.rows = sample_rows
+        rng = np.random.default_rng(0)
+        self.x = O.round_to(rng.standard_normal((1, sample_rows, H), dtype=np.float32), "f16")
+        self.w = O.round_to((1 + 0.1 * rng.standard_normal(H)).astype(np.float32), "f16")
+        cos, sin = O.rope_tables(sample_rows, D)
+        self.cos, self.sin = O.round_to(cos, "f16"), O.round_to(sin, "f16")
+        self.wg = O.round_to((0.02 * rng.standard_normal((I, H))).astype(np.float32), "f16")
+        self.wu = O.round_to((0.02 * rng.standard_normal((I, H))).astype(np.float32), "f16")
+
+    def step(self):
+        y = self.O.rmsnorm_rope(self.x, self.w, self.cos, self.sin, 1e-6, "f16")
+        return self.O.gated_mlp_f32(y, self.wg, self.wu, "silu", "f16")
+
+
+def cpu_cores():
+    return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+
+
+def cpu_baseline(sample_rows: int = 64, max_seconds: float = 15.0):
+    """Times the CPU path on a bounded row sample (reported beside the GPU number)."""
+    path = CpuPath(sample_rows)
+    path.step()  # warm-up
+    t0 = time.perf_counter()
+    n = 0
+    while n < 3 or (time.perf_counter() - t0 < max_seconds and n < 50):
+        path.step()
+        n += 1
+    dt = (time.perf_counter() - t0) / n
+    return {"value": sample_rows * FLOPS_PER_ROW / dt / 1e12, "unit": "TFLOP/s", "cores": cpu_cores(),
+            "kind": "port",
+            "sample": f"{sample_rows} of {ROWS} token rows per step (numpy fp32 RMSNorm+RoPE and gated-MLP "
+                      f"matmuls), {n} steps of {dt * 1e3:.1f} ms"}
+
+
+def run_reference(args):
+    """The reference's CPU implementation of the path (numpy restatement), rank 0 only."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    rows = 64
+    path = CpuPath(rows)
+    for _ in range(args.warmup):
+        path.step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        path.step()
+    dt = (time.perf_counter() - t0) / args.steps
+    value = rows * FLOPS_PER_ROW / dt / 1e12
+    sample = f"{rows} of {ROWS} token rows per step (numpy fp32 RMSNorm+RoPE and gated-MLP matmuls)"
+    line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ROWS * FLOPS_PER_ROW / (value * 1e12) * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(1,0.1) norm weight)",
+            "config": {"workload": "prefill RMSNorm+RoPE -> gated MLP (SiLU), x [8, 8192, 4096] fp16 row-sharded, "
+                                   "W_gate/W_up [11264, 4096] fp16, head_dim 64",
+                       "rows": ROWS, "hidden": H, "intermediate": I, "head_dim": D},
+            "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line))
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU step
+# ---------------------------------------------------------------------------
+def components(peaks, flush_buf):
+    """Per-op kernel numbers at the other configurations (rank 0)."""
+    import numpy as np
+    import torch
+
+    import triton_ops
+
+    out = {}
+    dev = torch.device("cuda")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    # RMSNorm+RoPE at [2, 128, 4096] (launch-latency bound; fits in L2)
+    x = torch.randn(2, 128, 4096, device=dev, dtype=torch.float16, generator=g)
+    w = (1 + 0.1 * torch.randn(4096, device=dev, generator=g)).half()
+    cos, sin = rope_tables(128, 64, dev)
+    ms = time_events(lambda: triton_ops.fused_rmsnorm_rope(x, w, cos, sin), 50, flush_buf)
+    nbytes = 2 * (2 * 128 * 4096 * 2) + 4096 * 2 + 2 * (128 * 32 * 2)
+    out["rmsnorm_rope_2x128x4096"] = {"us": ms * 1e3, "GB/s": nbytes / ms / 1e6}
+    # FP8 quantize / dequantize at [4096, 4096] with 0.1% outliers
+    t = torch.randn(4096, 4096, device=dev, generator=g).half()
+    idx = torch.randperm(t.numel(), device=dev, generator=g)[: t.numel() // 1000]
+    t.view(-1)[idx] = 200.0 * torch.sign(torch.randn(idx.numel(), device=dev, generator=g)).half()
+    q, s = triton_ops.quantize_fp8(t)
+    ms_q = time_events(lambda: triton_ops.quantize_fp8(t), 30, flush_buf)
+    ms_d = time_events(lambda: triton_ops.dequantize_fp8(q, s), 30, flush_buf)
+    nb = 3 * t.numel()
+    out["fp8_quantize_4096x4096"] = {"us": ms_q * 1e3, "GB/s": nb / ms_q / 1e6, "frac_hbm": nb / ms_q / 1e6 / peaks["hbm_gbs"]}
+    out["fp8_dequantize_4096x4096"] = {"us": ms_d * 1e3, "GB/s": nb / ms_d / 1e6, "frac_hbm": nb / ms_d / 1e6 / peaks["hbm_gbs"]}
+    # FP8 GEMM over M (reference codec, int8 tensor cores), N = K = 4096
+    b = torch.randn(4096, 4096, device=dev, generator=g).half()
+    qb, sb = triton_ops.quantize_fp8(b)
+    gemm = {}
+    for M in (16, 128, 1024, 4096, 8192):
+        a = torch.randn(M, 4096, device=dev, generator=g).half()
+        qa, sa = triton_ops.quantize_fp8(a)
+        ms = time_events(lambda: triton_ops.fp8_gemm(qa, qb, sa, sb), 20, flush_buf)
+        fl = 2.0 * M * 4096 * 4096
+        gemm[str(M)] = {"us": ms * 1e3, "TFLOP/s": fl / ms / 1e9}
+    out["fp8_gemm_Nx4096x4096"] = gemm
+    # gated MLP at [2, 1024, 4096] x [11264, 4096], SiLU and tanh-GELU
+    xm = torch.randn(2, 1024, 4096, device=dev, generator=g).half()
+    wg = (0.02 * torch.randn(11264, 4096, device=dev, generator=g)).half()
+    wu = (0.02 * torch.randn(11264, 4096, device=dev, generator=g)).half()
+    for act in ("silu", "gelu_tanh"):
+        ms = time_events(lambda: triton_ops.fused_gated_mlp(xm, wg, wu, act), 20, flush_buf)
+        fl = 4.0 * 2048 * 11264 * 4096
+        out[f"gated_mlp_2x1024x4096_{act}"] = {"us": ms * 1e3, "TFLOP/s": fl / ms / 1e9,
+                                                "frac_tensor_burst": fl / ms / 1e9 / peaks["bf16_tflops"]}
+    return out
+
+
+def read_traffic():
+    """DRAM bytes per launch of the gated-MLP kernel from the committed ncu summary, if present."""
+    p = ROOT / "profiles" / "gated_mlp_prefill_ncu.md"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_full_launch:"):
+            try:
+                return float(line.split(":", 1)[1].strip().split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def run_ours(args):
+    import torch
+
+    import triton_ops
+    from triton_ops import _lib
+    from triton_ops.sharding import broadcast_tensors, shard_rows, slab_tables
+
+    rank, world, local = dist_setup()
+    dev = torch.device("cuda", local)
+    peaks = measured_peaks()
+    shard = shard_rows(ROWS, world, rank)
+    rows = shard.rows
+
+    # weights + tables: made on rank 0, broadcast once (setup, untimed)
+    g = torch.Generator(device=dev).manual_seed(1234)
+    wg = (0.02 * torch.randn(I, H, device=dev, generator=g)).half()
+    wu = (0.02 * torch.randn(I, H, device=dev, generator=g)).half()
+    w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).half()
+    cos, sin = rope_tables(S, D, dev)
+    if world > 1:
+        broadcast_tensors([wg, wu, w, cos, sin], src=0)
+    cos_s, sin_s, nb, sl = slab_tables(cos, sin, shard, S)
+
+    # two input slabs, alternated, so a step never finds its input in L2
+    gx = torch.Generator(device=dev).manual_seed(99 + rank)
+    xs = [torch.randn(nb, sl, H, device=dev, generator=gx).half() for _ in range(2)]
+
+    def step(i):
+        yy = triton_ops.fused_rmsnorm_rope(xs[i % 2], w, cos_s, sin_s)
+        return triton_ops.fused_gated_mlp(yy, wg, wu, "silu")
+
+    st = torch.cuda.current_stream()
+    for i in range(args.warmup):
+        step(i)
+    torch.cuda.synchronize()
+    _lib.device_error_flags(clear=True)
+
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
+    launches0 = _lib.kernel_launches()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record(st)
+        for i in range(args.steps):
+            ev[i][0].record(st)
+            yy = triton_ops.fused_rmsnorm_rope(xs[i % 2], w, cos_s, sin_s)
+            ev[i][1].record(st)
+            triton_ops.fused_gated_mlp(yy, wg, wu, "silu")
+            ev[i][2].record(st)
+        t_end.record(st)
+        torch.cuda.synchronize()
+    barrier(world)
+    launches = _lib.kernel_launches() - launches0
+    elapsed_ms = t_start.elapsed_time(t_end)
+    rms_ms = sum(e[0].elapsed_time(e[1]) for e in ev) / args.steps
+    mlp_ms = sum(e[1].elapsed_time(e[2]) for e in ev) / args.steps
+    elapsed_ms = max_over_ranks(elapsed_ms, world)
+    rms_ms = max_over_ranks(rms_ms, world)
+    mlp_ms = max_over_ranks(mlp_ms, world)
+    clk = clocks.summary()
+    flags = _lib.device_error_flags(clear=True)
+
+    total_flops = ROWS * FLOPS_PER_ROW * args.steps
+    value = total_flops / (elapsed_ms / 1e3) / 1e12
+    mlp_flops_launch = rows * FLOPS_PER_ROW
+    rms_bytes_launch = rows * RMS_BYTES_PER_ROW + H * 2 + 2 * S * (D // 2) * 2
+
+    # ---- end to end: pinned host input in, host output out, every step ----
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty(nb, sl, H, dtype=torch.float16, pin_memory=True)
+        hx.copy_(xs[0].cpu())
+        hout = torch.empty(nb, sl, I, dtype=torch.float16, pin_memory=True)
+        dx = torch.empty_like(xs[0])
+        for _ in range(max(1, args.warmup // 2)):
+            dx.copy_(hx, non_blocking=True)
+            o = triton_ops.fused_gated_mlp(triton_ops.fused_rmsnorm_rope(dx, w, cos_s, sin_s), wg, wu, "silu")
+            hout.copy_(o, non_blocking=True)
+        torch.cuda.synchronize()
+        barrier(world)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(args.steps):
+            dx.copy_(hx, non_blocking=True)
+            o = triton_ops.fused_gated_mlp(triton_ops.fused_rmsnorm_rope(dx, w, cos_s, sin_s), wg, wu, "silu")
+            hout.copy_(o, non_blocking=True)
+        e1.record(st)
+        torch.cuda.synchronize()
+        barrier(world)
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+        e2e = {"value": total_flops / (e2e_ms / 1e3) / 1e12, "unit": "TFLOP/s",
+               "h2d_bytes_per_step": ROWS * H * 2, "d2h_bytes_per_step": ROWS * I * 2,
+               "ms_per_step": e2e_ms / args.steps}
+
+    comps = None
+    cpu = None
+    if rank == 0 and world == 1:
+        flush = torch.empty(256 * 2**20 // 4, dtype=torch.float32, device=dev)
+        if not args.no_components:
+            comps = components(peaks, flush)
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline()
+
+    if rank == 0:
+        mlp_tflops = mlp_flops_launch / (mlp_ms / 1e3) / 1e12
+        rms_gbs = rms_bytes_launch / (rms_ms / 1e3) / 1e9
+        traffic = read_traffic()
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": elapsed_ms / args.steps,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": "f16 (fp32 accumulate)",
+            "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(1,0.1) norm weight)",
+            "config": {
+                "workload": "prefill RMSNorm+RoPE -> gated MLP (SiLU), x [8, 8192, 4096] fp16 row-sharded, "
+                            "W_gate/W_up [11264, 4096] fp16, head_dim 64",
+                "rows": ROWS, "rows_per_rank": rows, "hidden": H, "intermediate": I, "head_dim": D,
+                "parallelism": f"rows{world}" if world > 1 else "single",
+                "l2": "inputs larger than L2: two alternating x slabs; per-step traffic > 4x L2",
+            },
+            "roofline": {
+                "bound": "tensor", "kernel": "gated_mlp (tcgen05 kind::f16)",
+                "achieved": mlp_tflops, "peak": peaks["bf16_tflops_sustained"], "unit": "TFLOP/s",
+                "frac": mlp_tflops / peaks["bf16_tflops_sustained"],
+                "peak_source": f"{peaks['source']} bf16_tflops_sustained",
+                "traffic": traffic,
+                "algorithmic_flops_per_launch": mlp_flops_launch,
+            },
+            "roofline_rmsnorm_rope": {
+                "bound": "hbm", "achieved": rms_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                "frac": rms_gbs / peaks["hbm_gbs"], "peak_source": f"{peaks['source']} hbm_gbs",
+                "algorithmic_bytes_per_launch": rms_bytes_launch, "us_per_launch": rms_ms * 1e3,
+            },
+            "e2e": e2e,
+            "gpu_launches": launches,
+            "clocks": clk,
+            "device_error_flags": flags,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        if comps is not None:
+            line["components"] = comps
+        print(json.dumps(line))
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-components", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

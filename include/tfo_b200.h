@@ -52,6 +52,10 @@ extern "C" {
 /* Library version string. */
 TFO_API const char* tfo_version(void);
 
+/* Number of kernels (and memsets) this library has launched in this process,
+ * over all devices and threads. No counterpart in the reference. */
+TFO_API unsigned long long tfo_kernel_launches(void);
+
 /* Message of the last failing call on this thread ("" if none). */
 TFO_API const char* tfo_last_error(void);
 

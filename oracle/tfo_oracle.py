@@ -228,6 +228,21 @@ def gated_mlp(x, w_gate, w_up, kind: str, x_dtype: str) -> np.ndarray:
     return round_to(out, x_dtype).reshape(*np.shape(x)[:-1], -1)
 
 
+def gated_mlp_f32(x, w_gate, w_up, kind: str, x_dtype: str) -> np.ndarray:
+    """The reference's arithmetic exactly as it runs on the CPU: fp32 projections
+    (F.linear on fp32-cast operands), fp32 activation, fp32 product, cast to x's
+    dtype (gated_mlp.py:238-251). Used as the timed CPU baseline."""
+    x2 = np.asarray(x, dtype=_F32).reshape(-1, np.shape(x)[-1])
+    g = x2 @ np.asarray(w_gate, dtype=_F32).T
+    u = x2 @ np.asarray(w_up, dtype=_F32).T
+    with np.errstate(over="ignore"):
+        if kind == "silu":
+            a = u / (_F32(1.0) + np.exp(-u))
+        else:
+            a = activation(u, kind).astype(_F32)
+    return round_to(g * a, x_dtype).reshape(*np.shape(x)[:-1], -1)
+
+
 # ---------------------------------------------------------------------------
 # synthetic inputs shared by the tests, bench and smoke
 # ---------------------------------------------------------------------------

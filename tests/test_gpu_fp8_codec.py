@@ -144,8 +144,16 @@ def test_overflow_handling(cuda):
     q, s = quantize_fp8_with_overflow_handling(t)
     assert s < 1.0
     assert torch.all(q == 255)
-    q2, s2 = quantize_fp8_with_overflow_handling(t, torch.tensor(4.0, device="cuda"))
-    assert s2.item() == 0.25  # 4 -> 2 -> 1 -> 0.5 -> 0.25: 1000 * 0.25 = 250 <= 448
+    # 1 -> 0.5 -> 0.25: 1000 * 0.25 = 250 <= 448 on the third check
+    q2, s2 = quantize_fp8_with_overflow_handling(t, torch.tensor(1.0, device="cuda"))
+    assert s2.item() == 0.25
+    np.testing.assert_array_equal(q2.cpu().numpy(), O.quantize_ref(host(t), 0.25))
+    # 4 -> 2 -> 1 -> 0.5: never in range after 3 halvings, as in the reference
+    from triton_ops.exceptions import NumericalOverflowError
+
+    with pytest.raises(NumericalOverflowError) as ei:
+        quantize_fp8_with_overflow_handling(t, torch.tensor(4.0, device="cuda"))
+    assert ei.value.attempts == 3 and ei.value.scale == 0.5
 
 
 def test_reference_round_trip_property(cuda):

@@ -1,5 +1,6 @@
 // C-ABI layer: argument checks, status/error reporting, device caches and
 // dispatch into the kernel translation units.
+#include <atomic>
 #include <mutex>
 #include <string>
 #include <tuple>
@@ -31,6 +32,9 @@ std::mutex g_cache_mu;
 std::map<int, int> g_sm_count;
 std::map<std::tuple<const void*, int, size_t, int>, int> g_occ;
 }  // namespace
+
+static std::atomic<unsigned long long> g_launches{0};
+void note_launch(int n) { g_launches.fetch_add(static_cast<unsigned long long>(n), std::memory_order_relaxed); }
 
 uint32_t* error_word_ptr() {
   int dev = 0;
@@ -103,6 +107,8 @@ __global__ void selftest_bounded_wait_kernel(long long budget, uint32_t* err) {
 using namespace tfo;
 
 extern "C" {
+
+unsigned long long tfo_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char* tfo_version(void) { return "tfo_b200 0.1.0 (sm_100a)"; }
 
@@ -229,6 +235,7 @@ int tfo_fp8_gemm(const void* a, const void* b, const float* a_scale, const float
   if (K == 0) {
     const size_t esz = out_dtype == F32 ? 4 : 2;
     e = cudaMemsetAsync(c, 0, static_cast<size_t>(M) * N * esz, st);
+    note_launch();
     if (e != cudaSuccess) return cuda_fail(e, "tfo_fp8_gemm");
     return TFO_OK;
   }
@@ -267,6 +274,7 @@ int tfo_gated_mlp(const void* x, const void* w_gate, const void* w_up, void* out
   if (K == 0) {
     const size_t esz = x_dtype == F32 ? 4 : 2;
     e = cudaMemsetAsync(out, 0, static_cast<size_t>(M) * N * esz, st);
+    note_launch();
     if (e != cudaSuccess) return cuda_fail(e, "tfo_gated_mlp");
     return TFO_OK;
   }
@@ -283,6 +291,7 @@ int tfo_selftest_bounded_wait(int64_t budget_cycles, void* stream) {
   if (budget_cycles <= 0 || budget_cycles > (1ll << 32))
     return fail(TFO_ERR_INVALID, "tfo_selftest_bounded_wait: budget must be in (0, 2^32] cycles");
   selftest_bounded_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(budget_cycles, error_word_ptr());
+  note_launch();
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "tfo_selftest_bounded_wait");
   return TFO_OK;

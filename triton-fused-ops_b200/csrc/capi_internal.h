@@ -10,6 +10,9 @@
 
 namespace tfo {
 
+// Counts kernel launches made by this library (reported by tfo_kernel_launches).
+void note_launch(int n = 1);
+
 // Device address of the current device's error word (cached per device).
 uint32_t* error_word_ptr();
 // Number of SMs of the current device (cached per device).

@@ -310,6 +310,7 @@ cudaError_t ensure_thresholds(cudaStream_t st) {
   if (e != cudaSuccess) return e;
   if (dev < 64 && __atomic_load_n(&g_thresh_ready[dev], __ATOMIC_ACQUIRE)) return cudaSuccess;
   init_thresholds_kernel<<<1, 160, 0, st>>>();
+  note_launch();
   e = cudaGetLastError();
   if (e == cudaSuccess && dev < 64) __atomic_store_n(&g_thresh_ready[dev], 1, __ATOMIC_RELEASE);
   return e;
@@ -331,11 +332,13 @@ cudaError_t amax_partials_launch(const void* x, int64_t n, int x_dtype, uint32_t
     case BF16: amax_partial_kernel<__nv_bfloat16><<<nparts, kAmaxThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), n, vec, partials); break;
     default: amax_partial_kernel<float><<<nparts, kAmaxThreads, 0, st>>>(static_cast<const float*>(x), n, vec, partials); break;
   }
+  note_launch();
   return cudaGetLastError();
 }
 
 cudaError_t finalize_scale_launch(const uint32_t* partials, int nparts, float* scale_out, cudaStream_t st) {
   finalize_scale_kernel<<<1, 256, 0, st>>>(partials, nparts, scale_out);
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -351,6 +354,7 @@ static cudaError_t enc_t(const void* x, int64_t n, const float* scale_in, const 
     encode_kernel<T, false><<<grid, kEncThreads, 0, st>>>(static_cast<const T*>(x), n, vec, scale_in, partials, nparts,
                                                           scale_out, static_cast<uint8_t*>(out));
   }
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -376,6 +380,7 @@ static cudaError_t dec_t(const void* q, int64_t n, bool e4m3, const float* scale
   } else {
     decode_kernel<TO, false><<<grid, kDecThreads, 0, st>>>(static_cast<const uint8_t*>(q), n, vec, scale, static_cast<TO*>(out));
   }
+  note_launch();
   return cudaGetLastError();
 }
 

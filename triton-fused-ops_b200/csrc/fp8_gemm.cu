@@ -163,6 +163,7 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
   kern<<<grid, 192, L::SMEM_BYTES, st>>>(ta, tb, tb, static_cast<int>(g.M), static_cast<int>(g.N),
                                           static_cast<int>(Kp), kGroupM, idesc, ep, error_word_ptr());
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -205,6 +206,7 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
     const int grid = static_cast<int>(std::min<int64_t>((total + prep_threads - 1) / prep_threads, num_sms() * 16));
     prep_rows_kernel<<<grid, prep_threads, 0, st>>>(a, g.M, g.K, g.K, da, p.Kp, flip,
                                                     (reinterpret_cast<uintptr_t>(a) & 15u) == 0 && g.K % 16 == 0);
+    note_launch();
     a = da;
   }
   if (p.prep_b) {
@@ -212,11 +214,13 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
     if (g.b_layout == 0) {
       dim3 grid(static_cast<unsigned>((g.N + 63) / 64), static_cast<unsigned>((p.Kp + 63) / 64));
       prep_transpose_kernel<<<grid, 256, 0, st>>>(b, g.K, g.N, db, p.Kp, flip);
+      note_launch();
     } else {
       const int64_t total = g.N * (p.Kp / 16);
       const int grid = static_cast<int>(std::min<int64_t>((total + prep_threads - 1) / prep_threads, num_sms() * 16));
       prep_rows_kernel<<<grid, prep_threads, 0, st>>>(b, g.N, g.K, g.K, db, p.Kp, flip,
                                                       (reinterpret_cast<uintptr_t>(b) & 15u) == 0 && g.K % 16 == 0);
+      note_launch();
     }
     b = db;
   }

@@ -151,6 +151,7 @@ cudaError_t launch_umma(const CUtensorMap& tx, const CUtensorMap& tg, const CUte
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
   kern<<<grid, 192, L::SMEM_BYTES, st>>>(tx, tg, tu, static_cast<int>(g.M), static_cast<int>(g.N),
                                           static_cast<int>(g.K), kGroupM, idesc, ep, error_word_ptr());
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -182,6 +183,7 @@ cudaError_t launch_simt_t(const GatedMlpArgs& g, cudaStream_t st) {
     case 1: gated_simt_kernel<TO, 1><<<grid, 256, 0, st>>>(g.x, g.wg, g.wu, static_cast<TO*>(g.out), g.M, g.N, g.K, g.x_dtype, g.w_dtype); break;
     default: gated_simt_kernel<TO, 2><<<grid, 256, 0, st>>>(g.x, g.wg, g.wu, static_cast<TO*>(g.out), g.M, g.N, g.K, g.x_dtype, g.w_dtype); break;
   }
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -196,6 +198,7 @@ cudaError_t launch_simt(const GatedMlpArgs& g, cudaStream_t st) {
 cudaError_t convert(const void* src, int64_t n, int dt, float* dst, cudaStream_t st) {
   const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, num_sms() * 8)));
   to_f32_kernel<<<grid, 256, 0, st>>>(src, n, dt, dst);
+  note_launch();
   return cudaGetLastError();
 }
 

@@ -293,6 +293,7 @@ cudaError_t launch_vec(const RmsNormRopeArgs& a, int threads, cudaStream_t st) {
       static_cast<TX*>(a.out), rows, static_cast<int>(a.seq_len), static_cast<int>(a.hidden),
       static_cast<int>(a.head_dim), static_cast<int>(a.num_heads * a.head_dim), a.cs_stride_seq, a.cs_stride_dim,
       a.eps, a.w_dtype);
+  note_launch();
   return cudaGetLastError();
 }
 
@@ -339,6 +340,7 @@ cudaError_t launch_generic(const RmsNormRopeArgs& a, cudaStream_t st) {
       static_cast<int>(a.seq_len), static_cast<int>(a.hidden), static_cast<int>(a.head_dim),
       static_cast<int>(a.num_heads * a.head_dim), a.cs_stride_seq, a.cs_stride_dim, a.eps, a.w_dtype, a.cos_dtype,
       a.sin_dtype);
+  note_launch();
   return cudaGetLastError();
 }
 

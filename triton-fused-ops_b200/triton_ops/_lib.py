@@ -49,6 +49,7 @@ _c_size = ctypes.c_size_t
 _SIGNATURES = {
     "tfo_version": (ctypes.c_char_p, []),
     "tfo_last_error": (ctypes.c_char_p, []),
+    "tfo_kernel_launches": (ctypes.c_ulonglong, []),
     "tfo_device_error_flags": (_c_int, [ctypes.POINTER(ctypes.c_uint32), _c_int]),
     "tfo_selftest_bounded_wait": (_c_int, [_c_i64, _c_vp]),
     "tfo_rmsnorm_rope": (
@@ -147,6 +148,11 @@ def device_error_flags(clear: bool = True) -> int:
     flags = ctypes.c_uint32(0)
     check(load().tfo_device_error_flags(ctypes.byref(flags), int(clear)), "tfo_device_error_flags")
     return int(flags.value)
+
+
+def kernel_launches() -> int:
+    """Kernels launched by the library so far in this process."""
+    return int(load().tfo_kernel_launches())
 
 
 def version() -> str:
