@@ -99,6 +99,24 @@ TFO_API int tfo_fp8_compute_scale(const void* x, int64_t numel, int x_dtype, flo
 TFO_API int tfo_fp8_quantize(const void* x, int64_t numel, int x_dtype, const float* scale, float* scale_out, void* out,
                      int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* tfo_fp8_quantize with a dynamic scale, for callers that cannot allocate
+ * device memory: code running inside another framework's memory pool or a
+ * fixed-budget serving process that owns every byte of the GPU, or a plugin
+ * whose host has no allocator to lend it. It calls no cudaMalloc, cudaFree or
+ * allocating library routine and takes no workspace: its scratch (the per-block
+ * amax partials) is a static 16 KiB device array inside this library, which
+ * every GPU that loads the library keeps until the process exits. Limit: a
+ * call may need at most 4096 partial slots (one per amax block, at most
+ * 8 x the SM count, i.e. 1184 on a 148-SM B200); larger needs are rejected with
+ * TFO_ERR_INVALID and an explanatory message. The first call on each device
+ * looks up the scratch address, so make it before any stream capture. All
+ * calls share the scratch: calls that overlap on the GPU (different streams,
+ * same device) race and must be serialised by the caller.
+ * No counterpart in the reference; same results as tfo_fp8_quantize with a
+ * NULL scale. */
+TFO_API int tfo_fp8_quantize_noalloc(const void* x, int64_t numel, int x_dtype, float* scale_out, void* out,
+                                     int out_dtype, void* stream);
+
 /* Dequantize numel codes (TFO_DTYPE_U8 reference codec or TFO_DTYPE_E4M3) to
  * out_dtype: out = dec(q) / scale.
  * Replaces: triton_ops/kernels/fp8_quantize.py:176-211 (dequantize_fp8) and

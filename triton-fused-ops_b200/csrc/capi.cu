@@ -33,6 +33,8 @@ std::map<int, int> g_sm_count;
 std::map<std::tuple<const void*, int, size_t, int>, int> g_occ;
 }  // namespace
 
+int report_error(int code, const char* msg) { return fail(code, msg); }
+
 static std::atomic<unsigned long long> g_launches{0};
 void note_launch(int n) { g_launches.fetch_add(static_cast<unsigned long long>(n), std::memory_order_relaxed); }
 

@@ -10,6 +10,9 @@
 
 namespace tfo {
 
+// Records `msg` as this thread's last error (read by tfo_last_error) and returns `code`.
+int report_error(int code, const char* msg);
+
 // Counts kernel launches made by this library (reported by tfo_kernel_launches).
 void note_launch(int n = 1);
 

@@ -14,8 +14,12 @@
 //                         derives the scale in double, CTA 0 publishes it,
 //                         then encodes its share of the tensor.
 // The second read of x is served by L2 for tensors that fit in it.
+#include <atomic>
+#include <string>
+
 #include "capi_internal.h"
 #include "common.cuh"
+#include "tfo_b200.h"
 
 namespace tfo {
 
@@ -394,4 +398,73 @@ cudaError_t dequantize_launch(const void* q, int64_t n, int q_dtype, const float
   }
 }
 
+// ---------------------------------------------------------------------------
+// Dynamic-scale quantize that allocates no device memory
+// ---------------------------------------------------------------------------
+// Scratch for the per-block amax partials of tfo_fp8_quantize_noalloc: a
+// file-scope device array, so every GPU that loads the library holds these
+// 16 KiB until the process exits. All calls share it and it keeps the last
+// call's contents; every slot a call reads is written by that same call's
+// amax kernel first, so nothing needs clearing.
+constexpr int kNoallocMaxPartials = 4096;
+static __device__ __align__(256) uint32_t g_noalloc_partials[kNoallocMaxPartials];
+
+namespace {
+// Device address of g_noalloc_partials per device. The array's name is only a
+// host-side stand-in in host code, so the address is looked up once per
+// device, with that device current, and passed to the kernels.
+std::atomic<uint32_t*> g_noalloc_ptr[64];
+
+cudaError_t noalloc_scratch(uint32_t** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  uint32_t* p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+  if (p == nullptr) {
+    void* addr = nullptr;
+    e = cudaGetSymbolAddress(&addr, g_noalloc_partials);
+    if (e != cudaSuccess) return e;
+    p = static_cast<uint32_t*>(addr);
+    g_noalloc_ptr[dev].store(p, std::memory_order_release);
+  }
+  *out = p;
+  return cudaSuccess;
+}
+}  // namespace
+
 }  // namespace tfo
+
+using tfo::report_error;
+
+extern "C" int tfo_fp8_quantize_noalloc(const void* x, int64_t numel, int x_dtype, float* scale_out, void* out,
+                                        int out_dtype, void* stream) {
+  using namespace tfo;
+  if (x_dtype != F16 && x_dtype != BF16 && x_dtype != F32)
+    return report_error(TFO_ERR_DTYPE, "tfo_fp8_quantize_noalloc: x must be f16, bf16 or f32");
+  if (out_dtype != U8 && out_dtype != E4M3)
+    return report_error(TFO_ERR_DTYPE, "tfo_fp8_quantize_noalloc: out must be U8 or E4M3");
+  if (numel < 0) return report_error(TFO_ERR_INVALID, "tfo_fp8_quantize_noalloc: negative numel");
+  if (!scale_out || (numel > 0 && (!x || !out)))
+    return report_error(TFO_ERR_INVALID, "tfo_fp8_quantize_noalloc: NULL pointer");
+  const int nparts = amax_partials_count(numel);
+  if (nparts > kNoallocMaxPartials)
+    return report_error(TFO_ERR_INVALID,
+                        "tfo_fp8_quantize_noalloc: this device needs more amax partial slots than the 4096 in the "
+                        "library's static scratch; use tfo_fp8_quantize with a caller-provided workspace");
+  uint32_t* parts = nullptr;
+  cudaError_t e = noalloc_scratch(&parts);
+  if (e != cudaSuccess) {
+    return report_error(TFO_ERR_CUDA, (std::string("tfo_fp8_quantize_noalloc: scratch address lookup failed: ") +
+                                       cudaGetErrorString(e)).c_str());
+  }
+  auto st = static_cast<cudaStream_t>(stream);
+  e = amax_partials_launch(x, numel, x_dtype, parts, nparts, st);
+  if (e == cudaSuccess) {
+    e = (numel == 0) ? finalize_scale_launch(parts, nparts, scale_out, st)
+                     : encode_launch(x, numel, x_dtype, nullptr, parts, nparts, scale_out, out, out_dtype, st);
+  }
+  if (e != cudaSuccess)
+    return report_error(TFO_ERR_CUDA, (std::string("tfo_fp8_quantize_noalloc: ") + cudaGetErrorString(e)).c_str());
+  return TFO_OK;
+}
