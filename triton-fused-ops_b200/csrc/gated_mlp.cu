@@ -219,7 +219,7 @@ cudaError_t gated_mlp_launch(const GatedMlpArgs& g, cudaStream_t st) {
         !make_tmap_kmajor(&tu, g.wu, dt, 2, g.N, g.K, g.K, kBlockN))
       return cudaErrorInvalidValue;
     const uint32_t fmt = (g.x_dtype == F16) ? 0u : 1u;
-    return launch_out<MmaKind::F16>(tx, tg, tu, g, make_idesc(1, fmt, fmt, false, false, 128, kBlockN), st);
+    return launch_out<MmaKind::F16>(tx, tg, tu, g, make_idesc(1, fmt, fmt, false, false, 128, 2 * kBlockN), st);
   }
 
   uint8_t* ws = static_cast<uint8_t*>(g.ws);
@@ -242,7 +242,7 @@ cudaError_t gated_mlp_launch(const GatedMlpArgs& g, cudaStream_t st) {
   if (!make_tmap_kmajor(&tx, x, dt, 4, g.M, g.K, g.K, 128) || !make_tmap_kmajor(&tg, wg, dt, 4, g.N, g.K, g.K, kBlockN) ||
       !make_tmap_kmajor(&tu, wu, dt, 4, g.N, g.K, g.K, kBlockN))
     return cudaErrorInvalidValue;
-  return launch_out<MmaKind::TF32>(tx, tg, tu, g, make_idesc(1, 2, 2, false, false, 128, kBlockN), st);
+  return launch_out<MmaKind::TF32>(tx, tg, tu, g, make_idesc(1, 2, 2, false, false, 128, 2 * kBlockN), st);
 }
 
 }  // namespace tfo

@@ -1,4 +1,5 @@
 // Persistent, warp-specialised tcgen05 GEMM mainloop for sm_100a.
+// `idesc` must describe an M = 128, N = NUM_B * BLOCK_N instruction.
 //
 //   D[m, n] (+)= sum_k A[m, k] * B_j[n, k]        for j < NUM_B
 //
@@ -54,7 +55,7 @@ struct GemmLayout {
   static constexpr int ACC_COLS = NUM_B * BLOCK_N;
   static constexpr int TMEM_COLS = 2 * ACC_COLS;
   static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns must be a power of two <= 512");
-  static_assert(BLOCK_N % 16 == 0 && BLOCK_N >= 16 && BLOCK_N <= 256, "UMMA N for M=128");
+  static_assert(BLOCK_N % 16 == 0 && BLOCK_N >= 16 && NUM_B * BLOCK_N <= 256, "UMMA N for M=128");
   // dynamic shared memory: ring + barriers + 1 KB for manual alignment
   static constexpr size_t SMEM_BYTES = static_cast<size_t>(STAGES) * STAGE_BYTES + 256 + 1024;
 };
@@ -165,14 +166,15 @@ __global__ void __launch_bounds__(192, 1)
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sa + s * L::A_BYTES);
           const uint32_t b_addr = smem_u32(sb + (s * NUM_B) * L::B_BYTES);
+          // The NUM_B B tiles of a stage are consecutive 128-byte-swizzled
+          // K-major tiles, i.e. one (NUM_B * BLOCK_N)-row tile, so a single
+          // UMMA of N = NUM_B * BLOCK_N reads the A tile once for all of them;
+          // accumulator column j * BLOCK_N + c belongs to B operand j.
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t adesc = smem_desc_kmajor_sw128(a_addr + kk * 32);
-#pragma unroll
-            for (int j = 0; j < NUM_B; ++j) {
-              const uint64_t bdesc = smem_desc_kmajor_sw128(b_addr + j * L::B_BYTES + kk * 32);
-              umma<KIND>(d_tmem + j * BLOCK_N, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
-            }
+            const uint64_t bdesc = smem_desc_kmajor_sw128(b_addr + kk * 32);
+            umma<KIND>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
           umma_commit(&empty[s]);
         }

@@ -10,12 +10,10 @@
 //   out[h*D + D/2 + i] = RN_x( y1*s + y2*c )
 // Columns at or past num_heads*D are written as y (normalised, not rotated).
 //
-// Fast path: one persistent CTA per SM slot streams whole rows; each thread
-// keeps NV 16-byte vectors of the row and its slice of `weight` (as fp32) in
-// registers, the sum of squares is a warp-shuffle + one-barrier block
-// reduction, and the rotate-half partner is fetched with one __shfl_xor per
-// 32-bit word. The next row's vectors are loaded before the current row is
-// reduced so every thread keeps two rows in flight.
+// Fast path: persistent CTAs stream whole rows through a shared-memory ring
+// filled by bulk copies (several rows in flight per CTA at no register cost);
+// the sum of squares is a warp-shuffle + one-barrier block reduction and the
+// rotate-half partner is fetched with one __shfl_xor per 32-bit word.
 #include "capi_internal.h"
 #include "common.cuh"
 
@@ -110,11 +108,19 @@ __device__ __forceinline__ float div_markstein(float a, float b, float rb) {
   return __fmaf_rn(r, rb, q0);
 }
 
-template <typename TX, typename TCS, int NV, bool CS_VEC, int MAXT>
-__global__ void __launch_bounds__(MAXT) rmsnorm_rope_vec_kernel(
+// Vector path. Each CTA owns rows blockIdx.x, blockIdx.x + gridDim.x, ...;
+// one thread streams them into a ring of `stages` row buffers in shared
+// memory with bulk copies (mbarrier completion), so the rows in flight cost
+// shared memory, not registers. Thread t handles the 16-byte vectors
+// g = v*T + t (v < NV) of each row; the weight row lives in shared memory as
+// fp32. The sum of squares is a warp-shuffle + one-barrier block reduction;
+// right after that barrier every thread has read its vectors of the slot, so
+// the slot is refilled with the row `stages` ahead.
+template <typename TX, typename TCS, int NV, bool CS_VEC>
+__global__ void __launch_bounds__(256) rmsnorm_rope_vec_kernel(
     const TX* __restrict__ x, const void* __restrict__ w, const TCS* __restrict__ cosp, const TCS* __restrict__ sinp,
     TX* __restrict__ out, int64_t rows, int seq_len, int hidden, int head_dim, int rot_cols, int64_t cs_ss,
-    int64_t cs_sd, float eps, int w_dtype) {
+    int64_t cs_sd, float eps, int w_dtype, int stages, uint32_t* err) {
   constexpr int E = Pack<TX>::E;
   const int T = blockDim.x;
   const int t = threadIdx.x;
@@ -123,54 +129,64 @@ __global__ void __launch_bounds__(MAXT) rmsnorm_rope_vec_kernel(
   const int dv = head_dim / E;     // vectors per head (power of two, <= 32)
   const int hv = dv >> 1;          // rotate-half partner distance, in vectors / lanes
   const int rot_vecs = rot_cols / E;
-  const float inv_h_num = static_cast<float>(hidden);
+  const uint32_t row_bytes = static_cast<uint32_t>(hidden) * sizeof(TX);
 
-  // weight slice, kept in registers for every row this CTA processes
-  float wr[NV][E];
-#pragma unroll
-  for (int v = 0; v < NV; ++v) {
-    const int g = v * T + t;
-#pragma unroll
-    for (int j = 0; j < E; ++j) wr[v][j] = (g < nvec) ? load_as_float(w, static_cast<int64_t>(g) * E + j, w_dtype) : 0.f;
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem);                 // [stages]
+  float* red = reinterpret_cast<float*>(smem + 8 * 8);                // [2][32]
+  float* wsm = reinterpret_cast<float*>(smem + 8 * 8 + 2 * 32 * 4);   // [hidden]
+  uint8_t* ring = smem + ((8 * 8 + 2 * 32 * 4 + hidden * 4 + 127) / 128) * 128;  // [stages][row_bytes]
+
+  const int64_t my_rows = (rows > blockIdx.x) ? (rows - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
+  if (t == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+    fence_mbar_init();
   }
-
-  __shared__ float red[2][32];
-  int buf = 0;
-
-  const uint4* xv = reinterpret_cast<const uint4*>(x);
-  uint4* ov = reinterpret_cast<uint4*>(out);
-  uint4 cur[NV], nxt[NV];
-  int64_t row = blockIdx.x;
-#pragma unroll
-  for (int v = 0; v < NV; ++v) {
-    const int g = v * T + t;
-    cur[v] = (row < rows && g < nvec) ? __ldcs(xv + row * nvec + g) : make_uint4(0, 0, 0, 0);
-  }
-
-  for (; row < rows; row += gridDim.x) {
-    const int64_t nrow = row + gridDim.x;
-#pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      const int g = v * T + t;
-      nxt[v] = (nrow < rows && g < nvec) ? __ldcs(xv + nrow * nvec + g) : make_uint4(0, 0, 0, 0);
+  for (int i = t; i < hidden; i += T) wsm[i] = load_as_float(w, i, w_dtype);
+  __syncthreads();
+  if (t == 0) {
+    for (int s = 0; s < stages && s < my_rows; ++s) {
+      const int64_t r = blockIdx.x + static_cast<int64_t>(s) * gridDim.x;
+      mbar_arrive_expect_tx(&full[s], row_bytes);
+      bulk_load(ring + static_cast<size_t>(s) * row_bytes, x + r * hidden, row_bytes, &full[s]);
     }
+  }
 
-    float xf[NV][E];
+  uint4* ov = reinterpret_cast<uint4*>(out);
+  int buf = 0;
+  for (int64_t i = 0; i < my_rows; ++i) {
+    const int64_t row = blockIdx.x + i * gridDim.x;
+    const int s = static_cast<int>(i % stages);
+    const uint32_t par = static_cast<uint32_t>((i / stages) & 1);
+    if (!mbar_wait(&full[s], par, err, ERR_WAIT_TIMEOUT_OTHER)) break;
+
+    const uint4* rv = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(s) * row_bytes);
+    uint4 cur[NV];
     float ss = 0.f;
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
-      Pack<TX>::unpack(cur[v], xf[v]);
+      const int g = v * T + t;
+      cur[v] = (g < nvec) ? rv[g] : make_uint4(0, 0, 0, 0);
+      float f[E];
+      Pack<TX>::unpack(cur[v], f);
 #pragma unroll
-      for (int j = 0; j < E; ++j) ss = __fmaf_rn(xf[v][j], xf[v][j], ss);
+      for (int j = 0; j < E; ++j) ss = __fmaf_rn(f[j], f[j], ss);
     }
     ss = warp_sum(ss);
-    if (lane == 0) red[buf][warp] = ss;
+    if (lane == 0) red[buf * 32 + warp] = ss;
     __syncthreads();
+    // every thread has consumed slot s: refill it with the row `stages` ahead
+    if (t == 0 && i + stages < my_rows) {
+      fence_proxy_async_smem();
+      const int64_t r = row + static_cast<int64_t>(stages) * gridDim.x;
+      mbar_arrive_expect_tx(&full[s], row_bytes);
+      bulk_load(ring + static_cast<size_t>(s) * row_bytes, x + r * hidden, row_bytes, &full[s]);
+    }
     float tot = 0.f;
-    for (int i = 0; i < nwarps; ++i) tot += red[buf][i];
+    for (int k = 0; k < nwarps; ++k) tot += red[buf * 32 + k];
     buf ^= 1;
 
-    const float ms = __fdiv_rn(tot, inv_h_num);
+    const float ms = __fdiv_rn(tot, static_cast<float>(hidden));
     const float rms = __fsqrt_rn(__fadd_rn(ms, eps));
     const bool fast_div = (rms > 0.f) && (rms <= 3.0e38f);  // finite, positive
     const float rb = __frcp_rn(rms);
@@ -179,19 +195,28 @@ __global__ void __launch_bounds__(MAXT) rmsnorm_rope_vec_kernel(
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
       const int g = v * T + t;
+      float xf[E];
+      Pack<TX>::unpack(cur[v], xf);
+      const float4* wv = reinterpret_cast<const float4*>(wsm + static_cast<int64_t>(min(g, nvec - 1)) * E);
+      float wr[E];
+#pragma unroll
+      for (int q = 0; q < E / 4; ++q) {
+        const float4 w4 = wv[q];
+        wr[4 * q] = w4.x; wr[4 * q + 1] = w4.y; wr[4 * q + 2] = w4.z; wr[4 * q + 3] = w4.w;
+      }
       // y = RN_x((x / rms) * w), kept both packed (to exchange) and as fp32
       float y[E];
 #pragma unroll
       for (int j = 0; j < E; ++j) {
-        const float q = fast_div ? div_markstein(xf[v][j], rms, rb) : __fdiv_rn(xf[v][j], rms);
-        y[j] = __fmul_rn(q, wr[v][j]);
+        const float q = fast_div ? div_markstein(xf[j], rms, rb) : __fdiv_rn(xf[j], rms);
+        y[j] = __fmul_rn(q, wr[j]);
       }
       uint32_t yw[4];
       pack_vec<TX, E>(y, yw);
       unpack_words<TX, E>(yw, y);
       uint32_t pw[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) pw[i] = __shfl_xor_sync(0xffffffffu, yw[i], hv);
+      for (int k = 0; k < 4; ++k) pw[k] = __shfl_xor_sync(0xffffffffu, yw[k], hv);
       if (g >= nvec) continue;
 
       float o[E];
@@ -201,15 +226,15 @@ __global__ void __launch_bounds__(MAXT) rmsnorm_rope_vec_kernel(
         const int hi = g & (dv - 1);
         const bool first = hi < hv;
         const int i0 = (first ? hi : hi - hv) * E;
-        float c[E], s[E];
+        float c[E], sn[E];
         load_cs<TCS, E, CS_VEC>(cosp + pos * cs_ss + i0 * cs_sd, cs_sd, c);
-        load_cs<TCS, E, CS_VEC>(sinp + pos * cs_ss + i0 * cs_sd, cs_sd, s);
+        load_cs<TCS, E, CS_VEC>(sinp + pos * cs_ss + i0 * cs_sd, cs_sd, sn);
         if (first) {
 #pragma unroll
-          for (int j = 0; j < E; ++j) o[j] = __fsub_rn(__fmul_rn(y[j], c[j]), __fmul_rn(p[j], s[j]));
+          for (int j = 0; j < E; ++j) o[j] = __fsub_rn(__fmul_rn(y[j], c[j]), __fmul_rn(p[j], sn[j]));
         } else {
 #pragma unroll
-          for (int j = 0; j < E; ++j) o[j] = __fadd_rn(__fmul_rn(p[j], s[j]), __fmul_rn(y[j], c[j]));
+          for (int j = 0; j < E; ++j) o[j] = __fadd_rn(__fmul_rn(p[j], sn[j]), __fmul_rn(y[j], c[j]));
         }
       } else {
 #pragma unroll
@@ -219,9 +244,14 @@ __global__ void __launch_bounds__(MAXT) rmsnorm_rope_vec_kernel(
       pack_vec<TX, E>(o, ow);
       __stcs(ov + row * nvec + g, make_uint4(ow[0], ow[1], ow[2], ow[3]));
     }
-#pragma unroll
-    for (int v = 0; v < NV; ++v) cur[v] = nxt[v];
   }
+}
+
+// Shared memory of the vector path: barriers + reduction slots + fp32 weight
+// row (128-byte aligned) + `stages` row buffers.
+inline size_t vec_smem_bytes(int hidden, int row_bytes, int stages) {
+  return ((8 * 8 + 2 * 32 * 4 + static_cast<size_t>(hidden) * 4 + 127) / 128) * 128 +
+         static_cast<size_t>(stages) * row_bytes;
 }
 
 // Generic path: any hidden size / head_dim / alignment. One CTA per row
@@ -282,17 +312,26 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_generic_kernel(
 // ---------------------------------------------------------------------------
 namespace {
 
-template <typename TX, typename TCS, int NV, bool CS_VEC, int MAXT>
+template <typename TX, typename TCS, int NV, bool CS_VEC>
 cudaError_t launch_vec(const RmsNormRopeArgs& a, int threads, cudaStream_t st) {
-  auto kern = rmsnorm_rope_vec_kernel<TX, TCS, NV, CS_VEC, MAXT>;
-  const int occ = cached_occupancy(reinterpret_cast<const void*>(kern), threads, 0);
+  auto kern = rmsnorm_rope_vec_kernel<TX, TCS, NV, CS_VEC>;
+  const int row_bytes = static_cast<int>(a.hidden * sizeof(TX));
+  // ring of up to 8 rows, about 48 KB, at least 2
+  const int stages = std::max(2, std::min(8, (48 * 1024) / row_bytes));
+  const size_t smem = vec_smem_bytes(static_cast<int>(a.hidden), row_bytes, stages);
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e != cudaSuccess) return e;
+  }
+  const int occ = cached_occupancy(reinterpret_cast<const void*>(kern), threads, smem);
   const int64_t rows = a.batch * a.seq_len;
   const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * std::max(occ, 1));
-  kern<<<static_cast<unsigned>(grid), threads, 0, st>>>(
+  kern<<<static_cast<unsigned>(grid), threads, smem, st>>>(
       static_cast<const TX*>(a.x), a.weight, static_cast<const TCS*>(a.cos), static_cast<const TCS*>(a.sin),
       static_cast<TX*>(a.out), rows, static_cast<int>(a.seq_len), static_cast<int>(a.hidden),
       static_cast<int>(a.head_dim), static_cast<int>(a.num_heads * a.head_dim), a.cs_stride_seq, a.cs_stride_dim,
-      a.eps, a.w_dtype);
+      a.eps, a.w_dtype, stages, error_word_ptr());
   note_launch();
   return cudaGetLastError();
 }
@@ -303,10 +342,10 @@ cudaError_t pick_nv(const RmsNormRopeArgs& a, int nvec, cudaStream_t st) {
     const int threads = ((nvec + nv - 1) / nv + 31) / 32 * 32;
     if (threads <= 256) {
       switch (nv) {
-        case 1: return launch_vec<TX, TCS, 1, CS_VEC, 256>(a, threads, st);
-        case 2: return launch_vec<TX, TCS, 2, CS_VEC, 256>(a, threads, st);
-        case 4: return launch_vec<TX, TCS, 4, CS_VEC, 256>(a, threads, st);
-        default: return launch_vec<TX, TCS, 8, CS_VEC, 256>(a, threads, st);
+        case 1: return launch_vec<TX, TCS, 1, CS_VEC>(a, threads, st);
+        case 2: return launch_vec<TX, TCS, 2, CS_VEC>(a, threads, st);
+        case 4: return launch_vec<TX, TCS, 4, CS_VEC>(a, threads, st);
+        default: return launch_vec<TX, TCS, 8, CS_VEC>(a, threads, st);
       }
     }
   }
