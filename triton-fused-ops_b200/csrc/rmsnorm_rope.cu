@@ -14,6 +14,8 @@
 // filled by bulk copies (several rows in flight per CTA at no register cost);
 // the sum of squares is a warp-shuffle + one-barrier block reduction and the
 // rotate-half partner is fetched with one __shfl_xor per 32-bit word.
+#include <type_traits>
+
 #include "capi_internal.h"
 #include "common.cuh"
 
@@ -82,23 +84,6 @@ __device__ __forceinline__ void unpack_words(const uint32_t (&w)[4], float (&f)[
   Pack<T>::unpack(u, f);
 }
 
-// Load E consecutive cos/sin entries starting at p as fp32.
-template <typename TCS, int E, bool CS_VEC>
-__device__ __forceinline__ void load_cs(const TCS* __restrict__ p, int64_t sd, float (&f)[E]) {
-  if constexpr (CS_VEC && sizeof(TCS) * E == 16) {
-    uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-    Pack<TCS>::unpack(u, f);
-  } else if constexpr (CS_VEC && sizeof(TCS) * E == 32) {  // fp32 tables, 8 entries
-    const float4* q = reinterpret_cast<const float4*>(p);
-    float4 a = __ldg(q), b = __ldg(q + 1);
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w;
-    f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-  } else {
-#pragma unroll
-    for (int j = 0; j < E; ++j) f[j] = Ty<TCS>::to_f(p[j * sd]);
-  }
-}
-
 // Correctly rounded a / b for finite a and finite b > 0, given rb = RN(1/b):
 // Markstein's FMA-corrected quotient (q0 = RN(a*rb), r = a - q0*b exactly,
 // q = RN(q0 + r*rb)). Three instructions instead of a full IEEE division.
@@ -113,29 +98,49 @@ __device__ __forceinline__ float div_markstein(float a, float b, float rb) {
 // memory with bulk copies (mbarrier completion), so the rows in flight cost
 // shared memory, not registers. Thread t handles the 16-byte vectors
 // g = v*T + t (v < NV) of each row; the weight row lives in shared memory as
-// fp32. The sum of squares is a warp-shuffle + one-barrier block reduction;
-// right after that barrier every thread has read its vectors of the slot, so
-// the slot is refilled with the row `stages` ahead.
-template <typename TX, typename TCS, int NV, bool CS_VEC>
-__global__ void __launch_bounds__(256) rmsnorm_rope_vec_kernel(
+// fp32, and before each row's reduction barrier the row's cos/sin entries are
+// converted to fp32 once into shared memory (double-buffered with the
+// reduction slots). The sum of squares is a warp-shuffle + one-barrier block
+// reduction; right after that barrier every thread has read its vectors of
+// the slot, so the slot is refilled with the row `stages` ahead.
+constexpr int kMaxHalfHead = 128;  // head_dim <= 256 on the vector path
+
+struct VecSmem {
+  static constexpr int kBar = 0;                           // uint64_t[8]
+  static constexpr int kRed = 64;                          // float[2][32]
+  static constexpr int kCs = kRed + 2 * 32 * 4;            // float[2][3 * kMaxHalfHead]: cos, sin, -sin
+  static constexpr int kW = kCs + 2 * 3 * kMaxHalfHead * 4;  // float[hidden]
+  __host__ __device__ static size_t ring_offset(int hidden) { return ((kW + static_cast<size_t>(hidden) * 4 + 127) / 128) * 128; }
+};
+
+// FULL: every thread owns exactly NV vectors of the row (NV * blockDim.x ==
+// hidden / E) and every column is rotated (num_heads * head_dim == hidden),
+// so no per-vector bounds or rotation checks are needed.
+template <typename TX, typename TCS, int NV, bool FULL>
+__global__ void __launch_bounds__(256, 4) rmsnorm_rope_vec_kernel(
     const TX* __restrict__ x, const void* __restrict__ w, const TCS* __restrict__ cosp, const TCS* __restrict__ sinp,
     TX* __restrict__ out, int64_t rows, int seq_len, int hidden, int head_dim, int rot_cols, int64_t cs_ss,
     int64_t cs_sd, float eps, int w_dtype, int stages, uint32_t* err) {
   constexpr int E = Pack<TX>::E;
+  // With 16-bit x and tables, y*c and p*s are exact in fp32, so the
+  // reference's RN(RN(y*c) -/+ RN(p*s)) equals one FMA on an exact product.
+  constexpr bool kExactProducts = sizeof(TX) == 2 && sizeof(TCS) == 2;
   const int T = blockDim.x;
   const int t = threadIdx.x;
   const int lane = t & 31, warp = t >> 5, nwarps = T >> 5;
   const int nvec = hidden / E;
   const int dv = head_dim / E;     // vectors per head (power of two, <= 32)
   const int hv = dv >> 1;          // rotate-half partner distance, in vectors / lanes
+  const int half = head_dim >> 1;
   const int rot_vecs = rot_cols / E;
   const uint32_t row_bytes = static_cast<uint32_t>(hidden) * sizeof(TX);
 
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem);                 // [stages]
-  float* red = reinterpret_cast<float*>(smem + 8 * 8);                // [2][32]
-  float* wsm = reinterpret_cast<float*>(smem + 8 * 8 + 2 * 32 * 4);   // [hidden]
-  uint8_t* ring = smem + ((8 * 8 + 2 * 32 * 4 + hidden * 4 + 127) / 128) * 128;  // [stages][row_bytes]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + VecSmem::kBar);
+  float* red = reinterpret_cast<float*>(smem + VecSmem::kRed);
+  float* csm = reinterpret_cast<float*>(smem + VecSmem::kCs);
+  float* wsm = reinterpret_cast<float*>(smem + VecSmem::kW);
+  uint8_t* ring = smem + VecSmem::ring_offset(hidden);
 
   const int64_t my_rows = (rows > blockIdx.x) ? (rows - blockIdx.x + gridDim.x - 1) / gridDim.x : 0;
   if (t == 0) {
@@ -152,27 +157,52 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_vec_kernel(
     }
   }
 
-  uint4* ov = reinterpret_cast<uint4*>(out);
-  int buf = 0;
-  for (int64_t i = 0; i < my_rows; ++i) {
-    const int64_t row = blockIdx.x + i * gridDim.x;
-    const int s = static_cast<int>(i % stages);
-    const uint32_t par = static_cast<uint32_t>((i / stages) & 1);
+  // Row-invariant per-vector offsets (shared-memory float offsets of the
+  // weight slice and of the cos / signed-sin entries within a cos-sin buffer).
+  int w_off[NV], c_off[NV], s_off[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int g = v * T + t;
+    w_off[v] = (FULL ? g : min(g, nvec - 1)) * E;
+    const int hi = g & (dv - 1);
+    const bool first = hi < hv;
+    c_off[v] = (first ? hi : hi - hv) * E;
+    s_off[v] = (first ? 2 * half : half) + c_off[v];
+  }
+
+  // ring slot, its phase parity and the RoPE position advance incrementally
+  // (no per-row 64-bit division)
+  int buf = 0, s = 0;
+  uint32_t par = 0;
+  int pos = static_cast<int>(blockIdx.x % static_cast<unsigned>(seq_len));
+  const int pos_step = static_cast<int>(gridDim.x % static_cast<unsigned>(seq_len));
+  int64_t row = blockIdx.x;
+  for (int64_t i = 0; i < my_rows; ++i, row += gridDim.x) {
+    // this row's cos, sin and -sin entries as fp32, published by the barrier below
+    for (int q = t; q < 2 * half; q += T) {
+      const int j = q < half ? q : q - half;
+      const float v = Ty<TCS>::to_f((q < half ? cosp : sinp)[static_cast<int64_t>(pos) * cs_ss + j * cs_sd]);
+      float* cs_buf = csm + buf * 3 * kMaxHalfHead;
+      cs_buf[q] = v;
+      if (q >= half) cs_buf[q + half] = -v;
+    }
     if (!mbar_wait(&full[s], par, err, ERR_WAIT_TIMEOUT_OTHER)) break;
 
     const uint4* rv = reinterpret_cast<const uint4*>(ring + static_cast<size_t>(s) * row_bytes);
-    uint4 cur[NV];
-    float ss = 0.f;
+    float xf[NV][E];
+    float ss0 = 0.f, ss1 = 0.f;
 #pragma unroll
     for (int v = 0; v < NV; ++v) {
       const int g = v * T + t;
-      cur[v] = (g < nvec) ? rv[g] : make_uint4(0, 0, 0, 0);
-      float f[E];
-      Pack<TX>::unpack(cur[v], f);
+      const uint4 u = (FULL || g < nvec) ? rv[g] : make_uint4(0, 0, 0, 0);
+      Pack<TX>::unpack(u, xf[v]);
 #pragma unroll
-      for (int j = 0; j < E; ++j) ss = __fmaf_rn(f[j], f[j], ss);
+      for (int j = 0; j < E; j += 2) {
+        ss0 = __fmaf_rn(xf[v][j], xf[v][j], ss0);
+        ss1 = __fmaf_rn(xf[v][j + 1], xf[v][j + 1], ss1);
+      }
     }
-    ss = warp_sum(ss);
+    float ss = warp_sum(ss0 + ss1);
     if (lane == 0) red[buf * 32 + warp] = ss;
     __syncthreads();
     // every thread has consumed slot s: refill it with the row `stages` ahead
@@ -182,76 +212,259 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_vec_kernel(
       mbar_arrive_expect_tx(&full[s], row_bytes);
       bulk_load(ring + static_cast<size_t>(s) * row_bytes, x + r * hidden, row_bytes, &full[s]);
     }
-    float tot = 0.f;
-    for (int k = 0; k < nwarps; ++k) tot += red[buf * 32 + k];
+    // second stage of the reduction: each warp sums the per-warp partials
+    const float tot = warp_sum(lane < nwarps ? red[buf * 32 + lane] : 0.f);
+    const float* cs_row = csm + buf * 3 * kMaxHalfHead;
     buf ^= 1;
 
     const float ms = __fdiv_rn(tot, static_cast<float>(hidden));
     const float rms = __fsqrt_rn(__fadd_rn(ms, eps));
-    const bool fast_div = (rms > 0.f) && (rms <= 3.0e38f);  // finite, positive
     const float rb = __frcp_rn(rms);
-    const int pos = static_cast<int>(row % seq_len);
+    uint4* orow = reinterpret_cast<uint4*>(out + row * hidden);
 
+    // Row-uniform choice of division: Markstein for finite positive rms,
+    // IEEE division otherwise (inf / NaN / zero rms, where x is not finite).
+    auto process = [&](auto fast_tag) {
+      constexpr bool FAST = decltype(fast_tag)::value;
 #pragma unroll
-    for (int v = 0; v < NV; ++v) {
-      const int g = v * T + t;
-      float xf[E];
-      Pack<TX>::unpack(cur[v], xf);
-      const float4* wv = reinterpret_cast<const float4*>(wsm + static_cast<int64_t>(min(g, nvec - 1)) * E);
-      float wr[E];
+      for (int v = 0; v < NV; ++v) {
+        const int g = v * T + t;
+        const float4* wv = reinterpret_cast<const float4*>(wsm + w_off[v]);
+        float y[E];
 #pragma unroll
-      for (int q = 0; q < E / 4; ++q) {
-        const float4 w4 = wv[q];
-        wr[4 * q] = w4.x; wr[4 * q + 1] = w4.y; wr[4 * q + 2] = w4.z; wr[4 * q + 3] = w4.w;
-      }
-      // y = RN_x((x / rms) * w), kept both packed (to exchange) and as fp32
-      float y[E];
+        for (int q4 = 0; q4 < E / 4; ++q4) {
+          const float4 w4 = wv[q4];
+          const float wr[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-      for (int j = 0; j < E; ++j) {
-        const float q = fast_div ? div_markstein(xf[j], rms, rb) : __fdiv_rn(xf[j], rms);
-        y[j] = __fmul_rn(q, wr[j]);
-      }
-      uint32_t yw[4];
-      pack_vec<TX, E>(y, yw);
-      unpack_words<TX, E>(yw, y);
-      uint32_t pw[4];
-#pragma unroll
-      for (int k = 0; k < 4; ++k) pw[k] = __shfl_xor_sync(0xffffffffu, yw[k], hv);
-      if (g >= nvec) continue;
-
-      float o[E];
-      if (g < rot_vecs) {
-        float p[E];
-        unpack_words<TX, E>(pw, p);
-        const int hi = g & (dv - 1);
-        const bool first = hi < hv;
-        const int i0 = (first ? hi : hi - hv) * E;
-        float c[E], sn[E];
-        load_cs<TCS, E, CS_VEC>(cosp + pos * cs_ss + i0 * cs_sd, cs_sd, c);
-        load_cs<TCS, E, CS_VEC>(sinp + pos * cs_ss + i0 * cs_sd, cs_sd, sn);
-        if (first) {
-#pragma unroll
-          for (int j = 0; j < E; ++j) o[j] = __fsub_rn(__fmul_rn(y[j], c[j]), __fmul_rn(p[j], sn[j]));
-        } else {
-#pragma unroll
-          for (int j = 0; j < E; ++j) o[j] = __fadd_rn(__fmul_rn(p[j], sn[j]), __fmul_rn(y[j], c[j]));
+          for (int j = 0; j < 4; ++j) {
+            const float xv = xf[v][4 * q4 + j];
+            const float q = FAST ? div_markstein(xv, rms, rb) : __fdiv_rn(xv, rms);
+            y[4 * q4 + j] = __fmul_rn(q, wr[j]);
+          }
         }
-      } else {
+        // y rounded to x's dtype: packed (to exchange) and back in fp32
+        uint32_t yw[4];
+        pack_vec<TX, E>(y, yw);
+        unpack_words<TX, E>(yw, y);
+        uint32_t pw[4];
 #pragma unroll
-        for (int j = 0; j < E; ++j) o[j] = y[j];
+        for (int k = 0; k < 4; ++k) pw[k] = __shfl_xor_sync(0xffffffffu, yw[k], hv);
+        if (!FULL && g >= nvec) continue;
+
+        if (FULL || g < rot_vecs) {
+          float pv[E];
+          unpack_words<TX, E>(pw, pv);
+          // first half: a*c - b*s; second half: b*s + a*c. With s taken from
+          // the negated copy for the first half, both are RN(RN(a*c) + RN(b*s')).
+          const float4* c4 = reinterpret_cast<const float4*>(cs_row + c_off[v]);
+          const float4* s4 = reinterpret_cast<const float4*>(cs_row + s_off[v]);
+          float o[E];
+#pragma unroll
+          for (int q4 = 0; q4 < E / 4; ++q4) {
+            const float4 cc = c4[q4], sv = s4[q4];
+            const float c[4] = {cc.x, cc.y, cc.z, cc.w};
+            const float sn[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float a = y[4 * q4 + j], b = pv[4 * q4 + j];
+              if constexpr (kExactProducts) {
+                o[4 * q4 + j] = __fmaf_rn(a, c[j], __fmul_rn(b, sn[j]));
+              } else {
+                o[4 * q4 + j] = __fadd_rn(__fmul_rn(a, c[j]), __fmul_rn(b, sn[j]));
+              }
+            }
+          }
+          uint32_t ow[4];
+          pack_vec<TX, E>(o, ow);
+          __stcs(orow + g, make_uint4(ow[0], ow[1], ow[2], ow[3]));
+        } else {
+          __stcs(orow + g, make_uint4(yw[0], yw[1], yw[2], yw[3]));
+        }
       }
-      uint32_t ow[4];
-      pack_vec<TX, E>(o, ow);
-      __stcs(ov + row * nvec + g, make_uint4(ow[0], ow[1], ow[2], ow[3]));
+    };
+    if (rms > 0.f && rms <= 3.0e38f) {
+      process(std::integral_constant<bool, true>{});
+    } else {
+      process(std::integral_constant<bool, false>{});
     }
+    if (++s == stages) {
+      s = 0;
+      par ^= 1u;
+    }
+    pos += pos_step;
+    if (pos >= seq_len) pos -= seq_len;
   }
 }
 
-// Shared memory of the vector path: barriers + reduction slots + fp32 weight
-// row (128-byte aligned) + `stages` row buffers.
+// Shared memory of the vector path: barriers, reduction and cos/sin slots,
+// the fp32 weight row and `stages` row buffers.
 inline size_t vec_smem_bytes(int hidden, int row_bytes, int stages) {
-  return ((8 * 8 + 2 * 32 * 4 + static_cast<size_t>(hidden) * 4 + 127) / 128) * 128 +
-         static_cast<size_t>(stages) * row_bytes;
+  return VecSmem::ring_offset(hidden) + static_cast<size_t>(stages) * row_bytes;
+}
+
+// Warp-per-row path (hidden = 32 * VPL vectors, VPL <= 16). Every warp owns
+// the rows gw, gw + GW, ... (gw = global warp id, GW = warps in the grid) and
+// one private row buffer in shared memory, filled by bulk copies, so no
+// CTA-wide barrier is needed after setup. The first pass moves the row from
+// shared memory into registers (VPL 16-byte vectors per lane) while summing
+// squares; lane 0 then immediately refills the buffer with the warp's next
+// row, whose load overlaps the second pass. The sum of squares is a pure
+// warp-shuffle reduction. Vector g = j*32 + lane; a head spans dv <= 32
+// vectors that divide 32, so a lane's position inside its head (and its
+// cos/sin offsets) is the same for every j.
+// At most 12 warps with 16 vectors per lane (row kept in 64 registers), 16 otherwise.
+constexpr int warp_rows_max_warps(int vpl) { return vpl >= 16 ? 12 : 16; }
+
+template <typename TX, typename TCS, bool FULLROT, int VPL>
+__global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope_warp_kernel(
+    const TX* __restrict__ x, const void* __restrict__ w, const TCS* __restrict__ cosp, const TCS* __restrict__ sinp,
+    TX* __restrict__ out, int64_t rows, int seq_len, int hidden, int head_dim, int rot_cols, int64_t cs_ss,
+    int64_t cs_sd, float eps, int w_dtype, int cs_stride, uint32_t* err) {
+  constexpr int E = Pack<TX>::E;
+  constexpr bool kExactProducts = sizeof(TX) == 2 && sizeof(TCS) == 2;
+  const int W = blockDim.x >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dv = head_dim / E;
+  const int hv = dv >> 1;
+  const int half = head_dim >> 1;
+  const int rot_vecs = rot_cols / E;
+  const uint32_t row_bytes = static_cast<uint32_t>(hidden) * sizeof(TX);
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                // [W]
+  float* wsm = reinterpret_cast<float*>(smem + 16 * 8);              // [hidden]
+  float* csm = wsm + hidden;                                         // [W][cs_stride]
+  uint8_t* ring = smem + ((16 * 8 + (static_cast<size_t>(hidden) + W * cs_stride) * 4 + 127) / 128) * 128;
+
+  uint64_t* full = bars + warp;
+  float* cs_buf = csm + warp * cs_stride;   // cos[half], sin[half], -sin[half]
+  uint8_t* slot = ring + static_cast<size_t>(warp) * row_bytes;
+  const uint4* rv = reinterpret_cast<const uint4*>(slot);
+
+  const int64_t gw = static_cast<int64_t>(blockIdx.x) * W + warp;
+  const int64_t GW = static_cast<int64_t>(gridDim.x) * W;
+  const int64_t my_rows = rows > gw ? (rows - gw + GW - 1) / GW : 0;
+
+  for (int i = threadIdx.x; i < hidden; i += blockDim.x) wsm[i] = load_as_float(w, i, w_dtype);
+  if (lane == 0) {
+    mbar_init(full, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (lane == 0 && my_rows > 0) {
+    mbar_arrive_expect_tx(full, row_bytes);
+    bulk_load(slot, x + gw * hidden, row_bytes, full);
+  }
+
+  // per-lane constants: position in head, cos / signed-sin offsets
+  const int hi = lane & (dv - 1);
+  const bool first = hi < hv;
+  const int c_off = (first ? hi : hi - hv) * E;
+  const int s_off = (first ? 2 * half : half) + c_off;
+
+  uint32_t par = 0;
+  int pos = static_cast<int>(gw % seq_len);
+  const int pos_step = static_cast<int>(GW % seq_len);
+  int64_t row = gw;
+  for (int64_t k = 0; k < my_rows; ++k, row += GW) {
+    for (int q = lane; q < 2 * half; q += 32) {
+      const int j = q < half ? q : q - half;
+      const float v = Ty<TCS>::to_f((q < half ? cosp : sinp)[static_cast<int64_t>(pos) * cs_ss + j * cs_sd]);
+      cs_buf[q] = v;
+      if (q >= half) cs_buf[q + half] = -v;
+    }
+    if (!mbar_wait(full, par, err, ERR_WAIT_TIMEOUT_OTHER)) break;
+    par ^= 1u;
+
+    uint4 xr[VPL];
+    float ss0 = 0.f, ss1 = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPL; ++j) {
+      xr[j] = rv[j * 32 + lane];
+      float f[E];
+      Pack<TX>::unpack(xr[j], f);
+#pragma unroll
+      for (int e = 0; e < E; e += 2) {
+        ss0 = __fmaf_rn(f[e], f[e], ss0);
+        ss1 = __fmaf_rn(f[e + 1], f[e + 1], ss1);
+      }
+    }
+    __syncwarp();  // all lanes have read the buffer: refill it with this warp's next row
+    if (lane == 0 && k + 1 < my_rows) {
+      fence_proxy_async_smem();
+      mbar_arrive_expect_tx(full, row_bytes);
+      bulk_load(slot, x + (row + GW) * hidden, row_bytes, full);
+    }
+    const float tot = warp_sum(ss0 + ss1);  // also orders this warp's cs_buf writes before the reads below
+    __syncwarp();
+    const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(hidden)), eps));
+    const float rb = __frcp_rn(rms);
+    uint4* orow = reinterpret_cast<uint4*>(out + row * hidden);
+    const float4* c4 = reinterpret_cast<const float4*>(cs_buf + c_off);
+    const float4* s4 = reinterpret_cast<const float4*>(cs_buf + s_off);
+
+    auto second_pass = [&](auto fast_tag) {
+      constexpr bool FAST = decltype(fast_tag)::value;
+#pragma unroll
+      for (int j = 0; j < VPL; ++j) {
+        const int g = j * 32 + lane;
+        float xf[E];
+        Pack<TX>::unpack(xr[j], xf);
+        const float4* wv = reinterpret_cast<const float4*>(wsm + g * E);
+        float y[E];
+#pragma unroll
+        for (int q4 = 0; q4 < E / 4; ++q4) {
+          const float4 w4 = wv[q4];
+          const float wr[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float xv = xf[4 * q4 + e];
+            const float qv = FAST ? div_markstein(xv, rms, rb) : __fdiv_rn(xv, rms);
+            y[4 * q4 + e] = __fmul_rn(qv, wr[e]);
+          }
+        }
+        uint32_t yw[4];
+        pack_vec<TX, E>(y, yw);
+        unpack_words<TX, E>(yw, y);
+        uint32_t pw[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) pw[q] = __shfl_xor_sync(0xffffffffu, yw[q], hv);
+        if (FULLROT || g < rot_vecs) {
+          float pv[E];
+          unpack_words<TX, E>(pw, pv);
+          float o[E];
+#pragma unroll
+          for (int q4 = 0; q4 < E / 4; ++q4) {
+            const float4 cc = c4[q4], sv = s4[q4];
+            const float c[4] = {cc.x, cc.y, cc.z, cc.w};
+            const float sn[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float a = y[4 * q4 + e], b = pv[4 * q4 + e];
+              if constexpr (kExactProducts) {
+                o[4 * q4 + e] = __fmaf_rn(a, c[e], __fmul_rn(b, sn[e]));
+              } else {
+                o[4 * q4 + e] = __fadd_rn(__fmul_rn(a, c[e]), __fmul_rn(b, sn[e]));
+              }
+            }
+          }
+          uint32_t ow[4];
+          pack_vec<TX, E>(o, ow);
+          __stcs(orow + g, make_uint4(ow[0], ow[1], ow[2], ow[3]));
+        } else {
+          __stcs(orow + g, make_uint4(yw[0], yw[1], yw[2], yw[3]));
+        }
+      }
+    };
+    if (rms > 0.f && rms <= 3.0e38f) {
+      second_pass(std::integral_constant<bool, true>{});
+    } else {
+      second_pass(std::integral_constant<bool, false>{});
+    }
+    __syncwarp();  // cs_buf is rewritten for the next row
+    pos += pos_step;
+    if (pos >= seq_len) pos -= seq_len;
+  }
 }
 
 // Generic path: any hidden size / head_dim / alignment. One CTA per row
@@ -312,12 +525,12 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_generic_kernel(
 // ---------------------------------------------------------------------------
 namespace {
 
-template <typename TX, typename TCS, int NV, bool CS_VEC>
+template <typename TX, typename TCS, int NV, bool FULL>
 cudaError_t launch_vec(const RmsNormRopeArgs& a, int threads, cudaStream_t st) {
-  auto kern = rmsnorm_rope_vec_kernel<TX, TCS, NV, CS_VEC>;
+  auto kern = rmsnorm_rope_vec_kernel<TX, TCS, NV, FULL>;
   const int row_bytes = static_cast<int>(a.hidden * sizeof(TX));
-  // ring of up to 8 rows, about 48 KB, at least 2
-  const int stages = std::max(2, std::min(8, (48 * 1024) / row_bytes));
+  // ring of up to 8 rows, about 32 KB, at least 2 (4 CTAs per SM at H = 4096 fp16)
+  const int stages = std::max(2, std::min(8, (32 * 1024) / row_bytes));
   const size_t smem = vec_smem_bytes(static_cast<int>(a.hidden), row_bytes, stages);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
@@ -336,16 +549,63 @@ cudaError_t launch_vec(const RmsNormRopeArgs& a, int threads, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-template <typename TX, typename TCS, bool CS_VEC>
+template <typename TX, typename TCS, bool FULLROT, int VPL>
+cudaError_t launch_warp_rows_t(const RmsNormRopeArgs& a, int warps, int cs_stride, size_t smem, cudaStream_t st) {
+  auto kern = rmsnorm_rope_warp_kernel<TX, TCS, FULLROT, VPL>;
+  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  const int64_t rows = a.batch * a.seq_len;
+  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((rows + warps - 1) / warps, num_sms()));
+  kern<<<static_cast<unsigned>(grid), warps * 32, smem, st>>>(
+      static_cast<const TX*>(a.x), a.weight, static_cast<const TCS*>(a.cos), static_cast<const TCS*>(a.sin),
+      static_cast<TX*>(a.out), rows, static_cast<int>(a.seq_len), static_cast<int>(a.hidden),
+      static_cast<int>(a.head_dim), static_cast<int>(a.num_heads * a.head_dim), a.cs_stride_seq, a.cs_stride_dim,
+      a.eps, a.w_dtype, cs_stride, error_word_ptr());
+  note_launch();
+  return cudaGetLastError();
+}
+
+// Warps per CTA (one CTA per SM, at most 16) so that the row buffers, the
+// fp32 weight row and the per-warp cos/sin buffers fit in shared memory.
+inline int warp_rows_config(int64_t hidden, int64_t head_dim, int elem, int max_warps, int* cs_stride, size_t* smem) {
+  const size_t row_bytes = static_cast<size_t>(hidden) * elem;
+  *cs_stride = static_cast<int>((3 * (head_dim / 2) + 3) / 4 * 4);
+  const size_t fixed = 16 * 8 + static_cast<size_t>(hidden) * 4 + 128;
+  const size_t per_warp = row_bytes + static_cast<size_t>(*cs_stride) * 4;
+  const size_t limit = 227 * 1024;
+  if (fixed + 8 * per_warp > limit) return 0;
+  const int warps = static_cast<int>(std::min<size_t>(max_warps, (limit - fixed) / per_warp));
+  *smem = ((16 * 8 + (static_cast<size_t>(hidden) + warps * *cs_stride) * 4 + 127) / 128) * 128 + warps * row_bytes;
+  return warps;
+}
+
+template <typename TX, typename TCS, int VPL>
+cudaError_t launch_warp_rows_v(const RmsNormRopeArgs& a, int warps, int cs_stride, size_t smem, cudaStream_t st) {
+  return (a.num_heads * a.head_dim == a.hidden) ? launch_warp_rows_t<TX, TCS, true, VPL>(a, warps, cs_stride, smem, st)
+                                                : launch_warp_rows_t<TX, TCS, false, VPL>(a, warps, cs_stride, smem, st);
+}
+
+template <typename TX, typename TCS>
+cudaError_t launch_warp_rows(const RmsNormRopeArgs& a, int vpl, int warps, int cs_stride, size_t smem, cudaStream_t st) {
+  switch (vpl) {
+    case 4: return launch_warp_rows_v<TX, TCS, 4>(a, warps, cs_stride, smem, st);
+    case 8: return launch_warp_rows_v<TX, TCS, 8>(a, warps, cs_stride, smem, st);
+    default: return launch_warp_rows_v<TX, TCS, 16>(a, warps, cs_stride, smem, st);
+  }
+}
+
+template <typename TX, typename TCS>
 cudaError_t pick_nv(const RmsNormRopeArgs& a, int nvec, cudaStream_t st) {
   for (int nv : {1, 2, 4, 8}) {
     const int threads = ((nvec + nv - 1) / nv + 31) / 32 * 32;
     if (threads <= 256) {
+      const bool full = (nv * threads == nvec) && (a.num_heads * a.head_dim == a.hidden);
       switch (nv) {
-        case 1: return launch_vec<TX, TCS, 1, CS_VEC>(a, threads, st);
-        case 2: return launch_vec<TX, TCS, 2, CS_VEC>(a, threads, st);
-        case 4: return launch_vec<TX, TCS, 4, CS_VEC>(a, threads, st);
-        default: return launch_vec<TX, TCS, 8, CS_VEC>(a, threads, st);
+        case 1: return full ? launch_vec<TX, TCS, 1, true>(a, threads, st) : launch_vec<TX, TCS, 1, false>(a, threads, st);
+        case 2: return full ? launch_vec<TX, TCS, 2, true>(a, threads, st) : launch_vec<TX, TCS, 2, false>(a, threads, st);
+        case 4: return full ? launch_vec<TX, TCS, 4, true>(a, threads, st) : launch_vec<TX, TCS, 4, false>(a, threads, st);
+        default: return full ? launch_vec<TX, TCS, 8, true>(a, threads, st) : launch_vec<TX, TCS, 8, false>(a, threads, st);
       }
     }
   }
@@ -353,12 +613,26 @@ cudaError_t pick_nv(const RmsNormRopeArgs& a, int nvec, cudaStream_t st) {
 }
 
 template <typename TX>
-cudaError_t dispatch_cs(const RmsNormRopeArgs& a, int nvec, bool cs_vec, cudaStream_t st) {
+cudaError_t dispatch_cs(const RmsNormRopeArgs& a, int nvec, cudaStream_t st) {
+  // warp-per-row kernel: 4, 8 or 16 vectors per lane, enough rows to fill the GPU
+  int cs_stride = 0;
+  size_t smem = 0;
+  const int vpl = nvec / 32;
+  const bool vpl_ok = (nvec % 32 == 0) && (vpl == 4 || vpl == 8 || vpl == 16);
+  const int warps =
+      vpl_ok ? warp_rows_config(a.hidden, a.head_dim, sizeof(TX), warp_rows_max_warps(vpl), &cs_stride, &smem) : 0;
+  if (warps > 0 && a.batch * a.seq_len >= 2ll * num_sms() * warps) {
+    switch (a.cos_dtype) {
+      case F16: return launch_warp_rows<TX, __half>(a, vpl, warps, cs_stride, smem, st);
+      case BF16: return launch_warp_rows<TX, __nv_bfloat16>(a, vpl, warps, cs_stride, smem, st);
+      default: return launch_warp_rows<TX, float>(a, vpl, warps, cs_stride, smem, st);
+    }
+  }
   switch (a.cos_dtype) {
-    case F16: return cs_vec ? pick_nv<TX, __half, true>(a, nvec, st) : pick_nv<TX, __half, false>(a, nvec, st);
+    case F16: return pick_nv<TX, __half>(a, nvec, st);
     case BF16:
-      return cs_vec ? pick_nv<TX, __nv_bfloat16, true>(a, nvec, st) : pick_nv<TX, __nv_bfloat16, false>(a, nvec, st);
-    default: return cs_vec ? pick_nv<TX, float, true>(a, nvec, st) : pick_nv<TX, float, false>(a, nvec, st);
+      return pick_nv<TX, __nv_bfloat16>(a, nvec, st);
+    default: return pick_nv<TX, float>(a, nvec, st);
   }
 }
 
@@ -396,14 +670,11 @@ cudaError_t rmsnorm_rope_launch(const RmsNormRopeArgs& a, cudaStream_t st) {
   bool vec = aligned16(a.x) && aligned16(a.out) && (a.hidden % E == 0) && (D % (2 * E) == 0) && dv >= 2 &&
              dv <= 32 && (dv & (dv - 1)) == 0 && (a.hidden / E) <= 8 * 256 && a.cos_dtype == a.sin_dtype;
   if (vec) {
-    const int csz = (a.cos_dtype == F32) ? 4 : 2;
-    const bool cs_vec = a.cs_stride_dim == 1 && aligned16(a.cos) && aligned16(a.sin) &&
-                        ((a.cs_stride_seq * csz) % 16 == 0) && ((E * csz) % 16 == 0);
     const int nvec = static_cast<int>(a.hidden / E);
     switch (a.x_dtype) {
-      case F16: return dispatch_cs<__half>(a, nvec, cs_vec, st);
-      case BF16: return dispatch_cs<__nv_bfloat16>(a, nvec, cs_vec, st);
-      default: return dispatch_cs<float>(a, nvec, cs_vec, st);
+      case F16: return dispatch_cs<__half>(a, nvec, st);
+      case BF16: return dispatch_cs<__nv_bfloat16>(a, nvec, st);
+      default: return dispatch_cs<float>(a, nvec, st);
     }
   }
   switch (a.x_dtype) {
