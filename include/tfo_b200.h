@@ -107,7 +107,7 @@ TFO_API int tfo_fp8_quantize(const void* x, int64_t numel, int x_dtype, const fl
  * amax partials) is a static 16 KiB device array inside this library, which
  * every GPU that loads the library keeps until the process exits. Limit: a
  * call may need at most 4096 partial slots (one per amax block, at most
- * 8 x the SM count, i.e. 1184 on a 148-SM B200); larger needs are rejected with
+ * 2 x the SM count, i.e. 296 on a 148-SM B200); larger needs are rejected with
  * TFO_ERR_INVALID and an explanatory message. The first call on each device
  * looks up the scratch address, so make it before any stream capture. All
  * calls share the scratch: calls that overlap on the GPU (different streams,

@@ -251,6 +251,20 @@ __device__ __forceinline__ uint64_t smem_desc_kmajor_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory matrix descriptor for an MN-major 8-bit operand tile stored
+// as [K rows][128 bytes of M/N] boxes with the 128-byte swizzle: 8-row
+// (1024-byte) atoms along K (SBO = 1024 bytes) and consecutive 128-byte-wide
+// M/N chunks `chunk_bytes` apart (LBO).
+__device__ __forceinline__ uint64_t smem_desc_mnmajor_sw128(uint32_t smem_addr, uint32_t chunk_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFF);           // start address
+  d |= static_cast<uint64_t>((chunk_bytes >> 4) & 0x3FFF) << 16;  // LBO: next 128-byte M/N chunk
+  d |= static_cast<uint64_t>(1024 >> 4) << 32;                     // SBO: next 8-row K group
+  d |= static_cast<uint64_t>(1) << 46;                             // descriptor version (sm_100)
+  d |= static_cast<uint64_t>(2) << 61;                             // layout: SWIZZLE_128B
+  return d;
+}
+
 // Instruction descriptor (dense, no negate). a_fmt/b_fmt/c_fmt follow the
 // tcgen05 encoding: kind::f16 {0 f16, 1 bf16, 2 tf32}; kind::i8 {0 u8, 1 s8};
 // kind::f8f6f4 {0 e4m3, 1 e5m2}; c_fmt {0 f16, 1 f32, 2 s32}.

@@ -23,30 +23,6 @@
 
 namespace tfo {
 
-// Exact thresholds of the reference codec in |c|: code k >= 1 is produced iff
-// |c| >= g_q_thresh[k]; g_q_thresh[0] = 0, g_q_thresh[128] = +inf.
-__device__ float g_q_thresh[129];
-
-// The reference codec magnitude for c >= 0 (the code is odd-symmetric).
-__device__ __forceinline__ int ref_code_exact(float c) {
-  const float t = __fmul_rn(__fdiv_rn(c, 448.0f), 127.0f);
-  return static_cast<int>(rintf(t));
-}
-
-// One thread per code: binary search for the smallest fp32 value producing it.
-__global__ void init_thresholds_kernel() {
-  const int k = threadIdx.x;
-  if (k > 128) return;
-  if (k == 0) { g_q_thresh[0] = 0.f; return; }
-  if (k == 128) { g_q_thresh[128] = __int_as_float(0x7f800000); return; }
-  uint32_t lo = 0, hi = __float_as_uint(448.0f);  // f(lo) < k <= f(hi)
-  while (hi - lo > 1) {
-    const uint32_t mid = lo + (hi - lo) / 2;
-    if (ref_code_exact(__uint_as_float(mid)) >= k) hi = mid; else lo = mid;
-  }
-  g_q_thresh[k] = __uint_as_float(hi);
-}
-
 __device__ __forceinline__ float min_nan(float a, float b) {
   float r;
   asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
@@ -58,18 +34,23 @@ __device__ __forceinline__ float max_nan(float a, float b) {
   return r;
 }
 
-// Reference-codec byte for scaled value c, using the threshold table in smem.
-// k0 = floor(|c|*127/448 + 0.5 - 2^-12) is k or k-1 (the margin dominates the
-// fp32 error of the estimate and sends exact .5 ties low), so one comparison
-// with the exact threshold finishes the job. NaN gives code 0 (byte 128), as
-// the reference's float->int8 conversion does.
-__device__ __forceinline__ uint32_t ref_encode(float c, const float* __restrict__ th) {
-  const float a = min_nan(fabsf(c), 448.0f);
-  const float u = __fmaf_rn(a, 0.28348214285714285f, 0.5f - 0.000244140625f);
-  int k = __float2int_rz(u);  // NaN -> 0
-  k += (a >= th[k + 1]) ? 1 : 0;
-  const int code = (c < 0.f) ? -k : k;
-  return static_cast<uint32_t>(code + 128) & 0xffu;
+// Reference-codec byte for a scaled value c:
+//   u = int8(rint(RN(RN(clamp(c, +-448) / 448) * 127))) + 128.
+// Since 448 = 7 * 2^6, RN(c / 448) = RN(c / 7) * 2^-6 exactly (a power-of-two
+// scaling commutes with rounding; where it would not, |c| is so small that
+// the code is 0 anyway), and RN(RN(c / 7) * 2^-6 * 127) = RN(RN(c / 7) * 1.984375)
+// because 127 / 64 = 1.984375 is exact. RN(c / 7) is Markstein's
+// FMA-corrected quotient with y = RN(1/7): q0 = RN(c*y), r = c - 7*q0 (exact),
+// q = RN(q0 + r*y). The clamp keeps NaN (it encodes as 0, like the
+// reference's float -> int8 conversion); +-inf clamp to +-448.
+__device__ __forceinline__ uint32_t ref_encode(float c) {
+  const float cl = min_nan(max_nan(c, -448.0f), 448.0f);
+  constexpr float kInv7 = 0.142857142857142857f;
+  const float q0 = __fmul_rn(cl, kInv7);
+  const float r = __fmaf_rn(-q0, 7.0f, cl);
+  const float q = __fmaf_rn(r, kInv7, q0);
+  const int k = __float2int_rn(__fmul_rn(q, 1.984375f));  // NaN -> 0, |k| <= 127
+  return static_cast<uint32_t>(k + 128) & 0xffu;
 }
 
 // ---- loading 16 elements as fp32 ------------------------------------------
@@ -135,11 +116,23 @@ __global__ void __launch_bounds__(kAmaxThreads) amax_partial_kernel(const T* __r
   int64_t done = 0;
   if (vec) {
     const int64_t n16 = n / 16;
-    for (int64_t i = tid; i < n16; i += stride) {
-      float f[16];
-      Load16<T>::template go<false>(x + i * 16, f);
+    // four independent 16-element loads in flight per thread
+    for (int64_t i = tid; i < n16; i += 4 * stride) {
+      float f[4][16];
 #pragma unroll
-      for (int j = 0; j < 16; ++j) m = max(m, __float_as_uint(fabsf(f[j])));
+      for (int u = 0; u < 4; ++u) {
+        const int64_t ii = i + u * stride;
+        if (ii < n16) {
+          Load16<T>::template go<false>(x + ii * 16, f[u]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 16; ++j) f[u][j] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int j = 0; j < 16; ++j) m = max(m, __float_as_uint(fabsf(f[u][j])));
     }
     done = n16 * 16;
   }
@@ -184,12 +177,8 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const T* __restrict
                                                              const float* __restrict__ scale_in,
                                                              const uint32_t* __restrict__ partials, int nparts,
                                                              float* __restrict__ scale_out, uint8_t* __restrict__ out) {
-  __shared__ float th[129];
   __shared__ float s_sh;
   __shared__ uint32_t red[kEncThreads / 32];
-  if (!E4M3) {
-    for (int i = threadIdx.x; i < 129; i += blockDim.x) th[i] = g_q_thresh[i];
-  }
   if (partials != nullptr) {
     const float s = reduce_partials_to_scale(partials, nparts, red);
     if (threadIdx.x == 0) {
@@ -208,7 +197,7 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const T* __restrict
       const float cl = min_nan(max_nan(c, -448.0f), 448.0f);
       return static_cast<uint32_t>(__nv_cvt_float_to_fp8(cl, __NV_SATFINITE, __NV_E4M3));
     } else {
-      return ref_encode(c, th);
+      return ref_encode(c);
     }
   };
 
@@ -256,7 +245,10 @@ template <typename TO, bool E4M3>
 __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __restrict__ q, int64_t n, bool vec,
                                                              const float* __restrict__ scale, TO* __restrict__ out) {
   using R = typename Raw<TO>::type;
-  __shared__ R lut[256];
+  // One copy of the 256 outputs per lane (lut[u * 32 + lane]), so the
+  // data-dependent lookups of a warp never collide on a shared-memory bank.
+  __shared__ R base[256];
+  __shared__ uint32_t lut[256 * 32];
   const float s = *scale;
   for (int u = threadIdx.x; u < 256; u += blockDim.x) {
     float v;
@@ -266,9 +258,12 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __re
     } else {
       v = __fmul_rn(__fdiv_rn(static_cast<float>(u - 128), 127.0f), 448.0f);
     }
-    lut[u] = to_raw<TO>(__fdiv_rn(v, s));
+    base[u] = to_raw<TO>(__fdiv_rn(v, s));
   }
   __syncthreads();
+  for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) lut[i] = base[i >> 5];
+  __syncthreads();
+  const uint32_t* my_lut = lut + (threadIdx.x & 31);
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   int64_t done = 0;
@@ -283,11 +278,11 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __re
         for (int k = 0; k < 8; ++k) {
           const uint32_t b0 = (w[k >> 1] >> (16 * (k & 1))) & 0xffu;
           const uint32_t b1 = (w[k >> 1] >> (16 * (k & 1) + 8)) & 0xffu;
-          o[k] = static_cast<uint32_t>(lut[b0]) | (static_cast<uint32_t>(lut[b1]) << 16);
+          o[k] = my_lut[b0 * 32] | (my_lut[b1 * 32] << 16);
         }
       } else {
 #pragma unroll
-        for (int k = 0; k < 16; ++k) o[k] = lut[(w[k >> 2] >> (8 * (k & 3))) & 0xffu];
+        for (int k = 0; k < 16; ++k) o[k] = my_lut[((w[k >> 2] >> (8 * (k & 3))) & 0xffu) * 32];
       }
       uint4* dst = reinterpret_cast<uint4*>(out) + i * (16 * sizeof(R) / 16);
 #pragma unroll
@@ -297,7 +292,7 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __re
     done = n16 * 16;
   }
   R* orow = reinterpret_cast<R*>(out);
-  for (int64_t i = done + tid; i < n; i += stride) orow[i] = lut[q[i]];
+  for (int64_t i = done + tid; i < n; i += stride) orow[i] = static_cast<R>(my_lut[q[i] * 32]);
 }
 
 // ---------------------------------------------------------------------------
@@ -306,27 +301,15 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __re
 namespace {
 bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int g_thresh_ready[64] = {0};
-
-cudaError_t ensure_thresholds(cudaStream_t st) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 64 && __atomic_load_n(&g_thresh_ready[dev], __ATOMIC_ACQUIRE)) return cudaSuccess;
-  init_thresholds_kernel<<<1, 160, 0, st>>>();
-  note_launch();
-  e = cudaGetLastError();
-  if (e == cudaSuccess && dev < 64) __atomic_store_n(&g_thresh_ready[dev], 1, __ATOMIC_RELEASE);
-  return e;
-}
-
 int grid_for(int64_t work_items, int threads, int per_sm) {
   const int64_t want = (work_items + threads - 1) / threads;
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, static_cast<int64_t>(num_sms()) * per_sm)));
 }
 }  // namespace
 
-int amax_partials_count(int64_t n) { return grid_for(std::max<int64_t>(n / 16, 1), kAmaxThreads, 8); }
+// Two amax CTAs per SM (each thread keeps four 16-element loads in flight),
+// so the encode kernel's CTAs each reduce at most 2 x SM-count partials.
+int amax_partials_count(int64_t n) { return grid_for(std::max<int64_t>(n / 64, 1), kAmaxThreads, 2); }
 
 cudaError_t amax_partials_launch(const void* x, int64_t n, int x_dtype, uint32_t* partials, int nparts,
                                  cudaStream_t st) {
@@ -364,10 +347,6 @@ static cudaError_t enc_t(const void* x, int64_t n, const float* scale_in, const 
 
 cudaError_t encode_launch(const void* x, int64_t n, int x_dtype, const float* scale_in, const uint32_t* partials,
                           int nparts, float* scale_out, void* out, int out_dtype, cudaStream_t st) {
-  if (out_dtype != E4M3) {
-    cudaError_t e = ensure_thresholds(st);
-    if (e != cudaSuccess) return e;
-  }
   switch (x_dtype) {
     case F16: return enc_t<__half>(x, n, scale_in, partials, nparts, scale_out, out, out_dtype, st);
     case BF16: return enc_t<__nv_bfloat16>(x, n, scale_in, partials, nparts, scale_out, out, out_dtype, st);
@@ -378,7 +357,8 @@ cudaError_t encode_launch(const void* x, int64_t n, int x_dtype, const float* sc
 template <typename TO>
 static cudaError_t dec_t(const void* q, int64_t n, bool e4m3, const float* scale, void* out, cudaStream_t st) {
   const bool vec = al16(q) && al16(out);
-  const int grid = grid_for(std::max<int64_t>(n / 16, 1), kDecThreads, 8);
+  // the per-lane tables take 33 KB of shared memory: 4 CTAs per SM
+  const int grid = grid_for(std::max<int64_t>(n / 16, 1), kDecThreads, 4);
   if (e4m3) {
     decode_kernel<TO, true><<<grid, kDecThreads, 0, st>>>(static_cast<const uint8_t*>(q), n, vec, scale, static_cast<TO*>(out));
   } else {

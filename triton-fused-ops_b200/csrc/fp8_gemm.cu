@@ -78,9 +78,65 @@ __global__ void __launch_bounds__(256) prep_transpose_kernel(const uint8_t* __re
   }
 }
 
+// Sign flip + sums for the single-operand staging of the reference codec.
+// Rows: dst[r, :] = src[r, :] ^ 0x80 (as int8) and sums[r] = sum of the
+// row's int8 values; one warp per row, K % 16 == 0, 16-byte aligned rows.
+__global__ void __launch_bounds__(256) prep_rows_s8_sum_kernel(const uint8_t* __restrict__ src, int64_t R, int64_t K,
+                                                               int8_t* __restrict__ dst, int32_t* __restrict__ sums) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < R; r += warps) {
+    const uint4* s4 = reinterpret_cast<const uint4*>(src + r * K);
+    uint4* d4 = reinterpret_cast<uint4*>(dst + r * K);
+    int acc = 0;
+    for (int64_t c = lane; c < K / 16; c += 32) {
+      uint4 u = __ldcs(s4 + c);
+      u.x ^= 0x80808080u; u.y ^= 0x80808080u; u.z ^= 0x80808080u; u.w ^= 0x80808080u;
+      acc = __dp4a(static_cast<int>(u.x), 0x01010101, acc);
+      acc = __dp4a(static_cast<int>(u.y), 0x01010101, acc);
+      acc = __dp4a(static_cast<int>(u.z), 0x01010101, acc);
+      acc = __dp4a(static_cast<int>(u.w), 0x01010101, acc);
+      d4[c] = u;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (lane == 0) sums[r] = acc;
+  }
+}
+
+// Columns: dst[k, n] = src[k, n] ^ 0x80 for a [K, N] matrix (N % 16 == 0) and
+// sums[n] += the column's int8 values over this block's K range (sums must be
+// zeroed first; integer atomics keep the result exact and order-independent).
+__global__ void __launch_bounds__(64) prep_cols_s8_sum_kernel(const uint8_t* __restrict__ src, int64_t K, int64_t N,
+                                                               int64_t k_per_block, int8_t* __restrict__ dst,
+                                                               int32_t* __restrict__ sums) {
+  const int64_t chunks = N / 16;
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (c >= chunks) return;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.y) * k_per_block;
+  const int64_t k1 = min(K, k0 + k_per_block);
+  int acc[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) acc[j] = 0;
+  for (int64_t k = k0; k < k1; ++k) {
+    uint4 u = __ldcs(reinterpret_cast<const uint4*>(src + k * N) + c);
+    u.x ^= 0x80808080u; u.y ^= 0x80808080u; u.z ^= 0x80808080u; u.w ^= 0x80808080u;
+    reinterpret_cast<uint4*>(dst + k * N)[c] = u;
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 16; ++j) acc[j] += static_cast<int8_t>((w[j >> 2] >> (8 * (j & 3))) & 0xffu);
+  }
+#pragma unroll
+  for (int j = 0; j < 16; ++j) atomicAdd(sums + c * 16 + j, acc[j]);
+}
+
 // ---------------------------------------------------------------------------
-// epilogue: scale and round
+// epilogue: correction, scale and round (or raw partials for split-K)
 // ---------------------------------------------------------------------------
+// With the reference codec, one operand may reach the tensor cores unflipped
+// (raw u8 = int8 value + 128); then acc = exact + 128 * (sum of the other
+// operand's int8 values along K), which corr_row (per output row, the A sums)
+// or corr_col (per output column, the B sums) removes.
 template <typename TO, bool INT_ACC>
 struct Fp8Epi {
   struct Params {
@@ -90,20 +146,74 @@ struct Fp8Epi {
     double codec_k;  // (448/127)^2 for the reference codec, 1 for e4m3
     int64_t ldc;
     bool vec_ok;
+    const int32_t* corr_row;
+    const int32_t* corr_col;
+    uint32_t* partial;  // split-K: [splits][M][N] raw accumulators
   };
   __device__ __forceinline__ void operator()(const Params& p, const uint32_t (&r)[1][16], int row, int col0, int M,
-                                             int N) const {
+                                             int N, int split) const {
     if (row >= M || col0 >= N) return;
+    const int valid = min(16, N - col0);
+    if (p.partial != nullptr) {
+      uint32_t* dst = p.partial + (static_cast<int64_t>(split) * M + row) * N + col0;
+      if (valid == 16 && (N & 3) == 0) {
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          reinterpret_cast<uint4*>(dst)[q] = make_uint4(r[0][4 * q], r[0][4 * q + 1], r[0][4 * q + 2], r[0][4 * q + 3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < valid) dst[i] = r[0][i];
+      }
+      return;
+    }
     const float alpha = static_cast<float>(p.codec_k / (static_cast<double>(__ldg(p.sa)) * __ldg(p.sb)));
+    const int32_t cr = p.corr_row ? 128 * __ldg(p.corr_row + row) : 0;
     float v[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) {
-      const float a = INT_ACC ? static_cast<float>(static_cast<int32_t>(r[0][i])) : __uint_as_float(r[0][i]);
+      float a;
+      if constexpr (INT_ACC) {
+        int32_t iv = static_cast<int32_t>(r[0][i]) - cr;
+        if (p.corr_col) iv -= 128 * __ldg(p.corr_col + min(col0 + i, N - 1));
+        a = static_cast<float>(iv);
+      } else {
+        a = __uint_as_float(r[0][i]);
+      }
       v[i] = a * alpha;
     }
-    store_row16<TO>(p.out + static_cast<int64_t>(row) * p.ldc + col0, v, min(16, N - col0), p.vec_ok);
+    store_row16<TO>(p.out + static_cast<int64_t>(row) * p.ldc + col0, v, valid, p.vec_ok);
   }
 };
+
+// Sums the split-K partials of each output, applies the correction and scale,
+// rounds to the output dtype.
+template <typename TO, bool INT_ACC>
+__global__ void __launch_bounds__(256) fp8_splitk_finalize_kernel(const uint32_t* __restrict__ partial, int splits,
+                                                                  int64_t M, int64_t N, const float* __restrict__ sa,
+                                                                  const float* __restrict__ sb, double codec_k,
+                                                                  const int32_t* __restrict__ corr_row,
+                                                                  const int32_t* __restrict__ corr_col,
+                                                                  TO* __restrict__ out) {
+  const float alpha = static_cast<float>(codec_k / (static_cast<double>(__ldg(sa)) * __ldg(sb)));
+  const int64_t total = M * N;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float v;
+    if constexpr (INT_ACC) {
+      int32_t acc = 0;
+      for (int s = 0; s < splits; ++s) acc += static_cast<int32_t>(partial[s * total + i]);
+      if (corr_row) acc -= 128 * corr_row[i / N];
+      if (corr_col) acc -= 128 * corr_col[i % N];
+      v = static_cast<float>(acc);
+    } else {
+      float acc = 0.f;
+      for (int s = 0; s < splits; ++s) acc += __uint_as_float(partial[s * total + i]);
+      v = acc;
+    }
+    out[i] = Ty<TO>::from_f(v * alpha);
+  }
+}
 
 // ---------------------------------------------------------------------------
 // host
@@ -114,37 +224,83 @@ constexpr int kStages = 4;
 constexpr int kGroupM = 16;
 
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Operand staging plan.
+//  * legacy: some operand is not TMA-addressable (unaligned base, K % 16 or,
+//    for a [K, N] B, N % 16): both operands are rewritten K-major, zero-padded
+//    and (reference codec) sign-flipped; B tiles K-major.
+//  * direct: both operands are read in place by TMA (B [K, N] as an MN-major
+//    operand). With the reference codec only the smaller operand is
+//    sign-flipped (with its sums for the epilogue correction); e4m3 needs none.
 struct Fp8Plan {
+  bool legacy;
   int64_t Kp;
-  bool prep_a, prep_b;
-  size_t off_a, off_b, bytes;
+  bool prep_a, prep_b;  // legacy: both; direct + codec: exactly one
+  bool b_mn;            // B read MN-major from [K, N]
+  size_t off_a, off_b, off_sum, off_part, bytes;
+  int bn, splits;
 };
 
-Fp8Plan plan_fp8(const Fp8GemmArgs& g) {
+int pick_block_n(int64_t M, int64_t N, bool b_mn) {
+  const int64_t mb = (M + 127) / 128;
+  if (N <= 128) return 128;
+  return (mb * ((N + 255) / 256) >= num_sms()) ? 256 : 128;
+  (void)b_mn;
+}
+
+Fp8Plan plan_fp8(const Fp8GemmArgs& g, bool assume_aligned) {
   Fp8Plan p{};
-  p.Kp = round_up(std::max<int64_t>(g.K, 1), 16);
   const bool codec = (g.ab_dtype == U8);
-  const bool a_aligned = (reinterpret_cast<uintptr_t>(g.a) & 15u) == 0 && g.K % 16 == 0;
-  const bool b_aligned = (reinterpret_cast<uintptr_t>(g.b) & 15u) == 0 && g.K % 16 == 0;
-  p.prep_a = codec || !a_aligned;
-  p.prep_b = codec || !b_aligned || g.b_layout == 0;
+  const bool a_ok = (assume_aligned || al16(g.a)) && g.K % 16 == 0;
+  const bool b_ok = (assume_aligned || al16(g.b)) && (g.b_layout == 1 ? g.K % 16 == 0 : g.N % 16 == 0);
+  p.legacy = !(a_ok && b_ok);
   size_t off = 0;
-  p.off_a = off;
-  if (p.prep_a) off += round_up(g.M * p.Kp, 256);
-  p.off_b = off;
-  if (p.prep_b) off += round_up(g.N * p.Kp, 256);
+  if (p.legacy) {
+    p.Kp = round_up(std::max<int64_t>(g.K, 1), 16);
+    p.prep_a = p.prep_b = true;
+    p.b_mn = false;
+    p.off_a = off;
+    off += round_up(g.M * p.Kp, 256);
+    p.off_b = off;
+    off += round_up(g.N * p.Kp, 256);
+    p.off_sum = off;
+  } else {
+    p.Kp = g.K;
+    p.b_mn = (g.b_layout == 0);
+    if (codec) {
+      p.prep_a = (g.M <= g.N);
+      p.prep_b = !p.prep_a;
+    }
+    p.off_a = off;
+    if (p.prep_a) off += round_up(g.M * g.K, 256);
+    p.off_b = off;
+    if (p.prep_b) off += round_up(g.N * g.K, 256);
+    p.off_sum = off;
+    if (codec) off += round_up(4 * (p.prep_a ? g.M : g.N), 256);
+  }
+  p.bn = pick_block_n(g.M, g.N, p.b_mn);
+  // split K when the tiles alone cannot occupy the GPU
+  const int64_t tiles = ((g.M + 127) / 128) * ((g.N + p.bn - 1) / p.bn);
+  const int64_t num_k = (p.Kp + 127) / 128;
+  p.splits = 1;
+  if (tiles < num_sms() / 2) {
+    p.splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_k / 4, num_sms() / tiles)));
+  }
+  p.off_part = off;
+  if (p.splits > 1) off += round_up(static_cast<int64_t>(p.splits) * g.M * g.N * 4, 256);
   p.bytes = off;
   return p;
 }
 
-template <MmaKind KIND, int BN, typename TO>
-cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, int64_t Kp,
+template <MmaKind KIND, int BN, typename TO, bool B_MN>
+cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, const Fp8Plan& p,
+                            uint32_t idesc, const int32_t* corr_row, const int32_t* corr_col, uint32_t* partial,
                             cudaStream_t st) {
   using L = GemmLayout<BN, 1, kStages>;
   constexpr bool INT_ACC = (KIND == MmaKind::I8);
   using Epi = Fp8Epi<TO, INT_ACC>;
-  auto kern = umma_gemm_kernel<KIND, BN, 1, kStages, Epi>;
+  auto kern = umma_gemm_kernel<KIND, BN, 1, kStages, Epi, B_MN>;
   static bool attr_set[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -154,92 +310,144 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
     if (e != cudaSuccess) return e;
     attr_set[dev] = true;
   }
-  typename Epi::Params ep{static_cast<TO*>(g.c), g.sa, g.sb,
-                          INT_ACC ? (448.0 / 127.0) * (448.0 / 127.0) : 1.0, g.N,
-                          (reinterpret_cast<uintptr_t>(g.c) & 15u) == 0 && (g.N * sizeof(TO)) % 16 == 0};
-  // kind::i8: D = s32, A = B = s8; kind::f8f6f4: D = f32, A = B = e4m3.
-  const uint32_t idesc = INT_ACC ? make_idesc(2, 1, 1, false, false, 128, BN) : make_idesc(1, 0, 0, false, false, 128, BN);
-  const int64_t tiles = ((g.M + 127) / 128) * ((g.N + BN - 1) / BN);
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
+  const double codec_k = INT_ACC ? (448.0 / 127.0) * (448.0 / 127.0) : 1.0;
+  typename Epi::Params ep{static_cast<TO*>(g.c), g.sa, g.sb, codec_k, g.N,
+                          al16(g.c) && (g.N * sizeof(TO)) % 16 == 0, corr_row, corr_col,
+                          p.splits > 1 ? partial : nullptr};
+  const int64_t work = ((g.M + 127) / 128) * ((g.N + BN - 1) / BN) * p.splits;
+  const int grid = static_cast<int>(std::min<int64_t>(work, num_sms()));
   kern<<<grid, 192, L::SMEM_BYTES, st>>>(ta, tb, tb, static_cast<int>(g.M), static_cast<int>(g.N),
-                                          static_cast<int>(Kp), kGroupM, idesc, ep, error_word_ptr());
+                                          static_cast<int>(p.Kp), kGroupM, idesc, ep, error_word_ptr(), p.splits);
+  note_launch();
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || p.splits == 1) return e;
+  const int64_t total = g.M * g.N;
+  const int fgrid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, num_sms() * 8)));
+  fp8_splitk_finalize_kernel<TO, INT_ACC><<<fgrid, 256, 0, st>>>(partial, p.splits, g.M, g.N, g.sa, g.sb, codec_k,
+                                                                 corr_row, corr_col, static_cast<TO*>(g.c));
   note_launch();
   return cudaGetLastError();
 }
 
-template <MmaKind KIND, int BN>
-cudaError_t launch_fp8_out(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, int64_t Kp,
-                           cudaStream_t st) {
+template <MmaKind KIND, int BN, bool B_MN>
+cudaError_t launch_fp8_out(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, const Fp8Plan& p,
+                           uint32_t idesc, const int32_t* cr, const int32_t* cc, uint32_t* part, cudaStream_t st) {
   switch (g.out_dtype) {
-    case F16: return launch_fp8_gemm<KIND, BN, __half>(ta, tb, g, Kp, st);
-    case BF16: return launch_fp8_gemm<KIND, BN, __nv_bfloat16>(ta, tb, g, Kp, st);
-    default: return launch_fp8_gemm<KIND, BN, float>(ta, tb, g, Kp, st);
+    case F16: return launch_fp8_gemm<KIND, BN, __half, B_MN>(ta, tb, g, p, idesc, cr, cc, part, st);
+    case BF16: return launch_fp8_gemm<KIND, BN, __nv_bfloat16, B_MN>(ta, tb, g, p, idesc, cr, cc, part, st);
+    default: return launch_fp8_gemm<KIND, BN, float, B_MN>(ta, tb, g, p, idesc, cr, cc, part, st);
   }
+}
+
+template <MmaKind KIND, bool B_MN>
+cudaError_t launch_fp8_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, const Fp8Plan& p,
+                          uint32_t idesc, const int32_t* cr, const int32_t* cc, uint32_t* part, cudaStream_t st) {
+  return p.bn == 256 ? launch_fp8_out<KIND, 256, B_MN>(ta, tb, g, p, idesc, cr, cc, part, st)
+                     : launch_fp8_out<KIND, 128, B_MN>(ta, tb, g, p, idesc, cr, cc, part, st);
 }
 
 }  // namespace
 
-// Upper bound over operand alignments: room for both prepared operands.
+// Upper bound over operand alignments.
 size_t fp8_gemm_workspace_bytes(const Fp8GemmArgs& g) {
-  const int64_t Kp = round_up(std::max<int64_t>(g.K, 1), 16);
-  return static_cast<size_t>(round_up(g.M * Kp, 256) + round_up(g.N * Kp, 256));
+  Fp8GemmArgs u = g;
+  const Fp8Plan a = plan_fp8(u, true);
+  u.K = round_up(std::max<int64_t>(g.K, 1), 16) + 1;  // forces the legacy plan's sizes
+  Fp8Plan b = plan_fp8(u, false);
+  b.bytes = round_up(g.M * round_up(std::max<int64_t>(g.K, 1), 16), 256) +
+            round_up(g.N * round_up(std::max<int64_t>(g.K, 1), 16), 256) + (b.bytes - b.off_part);
+  return std::max(a.bytes, b.bytes);
 }
 
-// Static tile table: BLOCK_N = 256 once there are enough row blocks to fill the
-// GPU, 128 for short-M problems (more column tiles in flight).
-int fp8_gemm_block_n(int64_t M, int64_t N) {
-  const int64_t mb = (M + 127) / 128;
-  return (mb * ((N + 255) / 256) >= num_sms() || N <= 128) ? (N <= 128 ? 128 : 256) : 128;
-}
+int fp8_gemm_block_n(int64_t M, int64_t N) { return pick_block_n(M, N, false); }
 
 cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
-  const Fp8Plan p = plan_fp8(g);
+  const Fp8Plan p = plan_fp8(g, false);
   if (g.ws_bytes < p.bytes || (p.bytes > 0 && g.ws == nullptr)) return cudaErrorInvalidValue;
   uint8_t* ws = static_cast<uint8_t*>(g.ws);
-  const uint32_t flip = (g.ab_dtype == U8) ? 0x80u : 0u;
+  const bool codec = (g.ab_dtype == U8);
   const uint8_t* a = static_cast<const uint8_t*>(g.a);
   const uint8_t* b = static_cast<const uint8_t*>(g.b);
+  const int32_t* corr_row = nullptr;
+  const int32_t* corr_col = nullptr;
+  uint32_t* partial = reinterpret_cast<uint32_t*>(ws + p.off_part);
   const int prep_threads = 256;
-  if (p.prep_a) {
+  cudaError_t e = cudaSuccess;
+  // A and B tensor-core formats: kind::i8 {0 u8, 1 s8}, kind::f8f6f4 {0 e4m3}
+  uint32_t a_fmt = codec ? 1u : 0u, b_fmt = codec ? 1u : 0u;
+
+  if (p.legacy) {
+    const uint32_t flip = codec ? 0x80u : 0u;
     uint8_t* da = ws + p.off_a;
-    const int64_t total = g.M * (p.Kp / 16);
-    const int grid = static_cast<int>(std::min<int64_t>((total + prep_threads - 1) / prep_threads, num_sms() * 16));
-    prep_rows_kernel<<<grid, prep_threads, 0, st>>>(a, g.M, g.K, g.K, da, p.Kp, flip,
-                                                    (reinterpret_cast<uintptr_t>(a) & 15u) == 0 && g.K % 16 == 0);
+    const int64_t total_a = g.M * (p.Kp / 16);
+    const int grid_a = static_cast<int>(std::min<int64_t>((total_a + prep_threads - 1) / prep_threads, num_sms() * 16));
+    prep_rows_kernel<<<grid_a, prep_threads, 0, st>>>(a, g.M, g.K, g.K, da, p.Kp, flip, al16(a) && g.K % 16 == 0);
     note_launch();
     a = da;
-  }
-  if (p.prep_b) {
     uint8_t* db = ws + p.off_b;
     if (g.b_layout == 0) {
       dim3 grid(static_cast<unsigned>((g.N + 63) / 64), static_cast<unsigned>((p.Kp + 63) / 64));
       prep_transpose_kernel<<<grid, 256, 0, st>>>(b, g.K, g.N, db, p.Kp, flip);
       note_launch();
     } else {
-      const int64_t total = g.N * (p.Kp / 16);
-      const int grid = static_cast<int>(std::min<int64_t>((total + prep_threads - 1) / prep_threads, num_sms() * 16));
-      prep_rows_kernel<<<grid, prep_threads, 0, st>>>(b, g.N, g.K, g.K, db, p.Kp, flip,
-                                                      (reinterpret_cast<uintptr_t>(b) & 15u) == 0 && g.K % 16 == 0);
+      const int64_t total_b = g.N * (p.Kp / 16);
+      const int grid_b = static_cast<int>(std::min<int64_t>((total_b + prep_threads - 1) / prep_threads, num_sms() * 16));
+      prep_rows_kernel<<<grid_b, prep_threads, 0, st>>>(b, g.N, g.K, g.K, db, p.Kp, flip, al16(b) && g.K % 16 == 0);
       note_launch();
     }
     b = db;
+  } else if (codec && p.prep_a) {
+    int32_t* sums = reinterpret_cast<int32_t*>(ws + p.off_sum);
+    int8_t* da = reinterpret_cast<int8_t*>(ws + p.off_a);
+    const int grid = static_cast<int>(std::min<int64_t>((g.M + 7) / 8, num_sms() * 8));
+    prep_rows_s8_sum_kernel<<<grid, 256, 0, st>>>(a, g.M, g.K, da, sums);
+    note_launch();
+    a = reinterpret_cast<const uint8_t*>(da);
+    corr_row = sums;
+    b_fmt = 0;  // B stays raw u8
+  } else if (codec && p.prep_b) {
+    int32_t* sums = reinterpret_cast<int32_t*>(ws + p.off_sum);
+    int8_t* db = reinterpret_cast<int8_t*>(ws + p.off_b);
+    if (g.b_layout == 0) {
+      e = cudaMemsetAsync(sums, 0, static_cast<size_t>(g.N) * 4, st);
+      note_launch();
+      if (e != cudaSuccess) return e;
+      // 64 column chunks (1024 columns) x 32 K rows per CTA: >= 8 CTAs per SM for 4096 x 4096
+      const int64_t chunks = g.N / 16;
+      const int64_t kpb = 32;
+      dim3 grid(static_cast<unsigned>((chunks + 63) / 64), static_cast<unsigned>((g.K + kpb - 1) / kpb));
+      prep_cols_s8_sum_kernel<<<grid, 64, 0, st>>>(b, g.K, g.N, kpb, db, sums);
+      note_launch();
+    } else {
+      const int grid = static_cast<int>(std::min<int64_t>((g.N + 7) / 8, num_sms() * 8));
+      prep_rows_s8_sum_kernel<<<grid, 256, 0, st>>>(b, g.N, g.K, db, sums);
+      note_launch();
+    }
+    b = reinterpret_cast<const uint8_t*>(db);
+    corr_col = sums;
+    a_fmt = 0;  // A stays raw u8
   }
-  cudaError_t e = cudaGetLastError();
+  e = cudaGetLastError();
   if (e != cudaSuccess) return e;
 
-  const int bn = fp8_gemm_block_n(g.M, g.N);
   CUtensorMap ta, tb;
-  const int64_t lda = p.prep_a ? p.Kp : g.K;
-  const int64_t ldb = p.prep_b ? p.Kp : g.K;
-  if (!make_tmap_kmajor(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.M, p.prep_a ? p.Kp : g.K, lda, 128) ||
-      !make_tmap_kmajor(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.N, p.prep_b ? p.Kp : g.K, ldb, bn))
-    return cudaErrorInvalidValue;
-  const int64_t Kp = p.Kp;
-  if (g.ab_dtype == U8) {
-    return bn == 256 ? launch_fp8_out<MmaKind::I8, 256>(ta, tb, g, Kp, st) : launch_fp8_out<MmaKind::I8, 128>(ta, tb, g, Kp, st);
+  const int64_t lda = p.legacy ? p.Kp : g.K;
+  if (!make_tmap_kmajor(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.M, lda, lda, 128)) return cudaErrorInvalidValue;
+  if (p.b_mn) {
+    // [K, N] with N contiguous: boxes of 128 bytes of N x 128 K rows
+    if (!make_tmap_kmajor(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.N, g.N, 128)) return cudaErrorInvalidValue;
+  } else {
+    const int64_t ldb = p.legacy ? p.Kp : g.K;
+    if (!make_tmap_kmajor(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.N, ldb, ldb, p.bn)) return cudaErrorInvalidValue;
   }
-  return bn == 256 ? launch_fp8_out<MmaKind::F8F6F4, 256>(ta, tb, g, Kp, st)
-                   : launch_fp8_out<MmaKind::F8F6F4, 128>(ta, tb, g, Kp, st);
+  const uint32_t c_fmt = codec ? 2u : 1u;  // s32 / f32 accumulators
+  const uint32_t idesc = make_idesc(c_fmt, a_fmt, b_fmt, false, p.b_mn, 128, p.bn);
+  if (codec) {
+    return p.b_mn ? launch_fp8_bn<MmaKind::I8, true>(ta, tb, g, p, idesc, corr_row, corr_col, partial, st)
+                  : launch_fp8_bn<MmaKind::I8, false>(ta, tb, g, p, idesc, corr_row, corr_col, partial, st);
+  }
+  return p.b_mn ? launch_fp8_bn<MmaKind::F8F6F4, true>(ta, tb, g, p, idesc, nullptr, nullptr, partial, st)
+                : launch_fp8_bn<MmaKind::F8F6F4, false>(ta, tb, g, p, idesc, nullptr, nullptr, partial, st);
 }
 
 }  // namespace tfo

@@ -44,7 +44,7 @@ struct GatedEpi {
     bool vec_ok;
   };
   __device__ __forceinline__ void operator()(const Params& p, const uint32_t (&r)[2][16], int row, int col0, int M,
-                                             int N) const {
+                                             int N, int /*split*/) const {
     if (row >= M || col0 >= N) return;
     float v[16];
 #pragma unroll
@@ -150,7 +150,7 @@ cudaError_t launch_umma(const CUtensorMap& tx, const CUtensorMap& tg, const CUte
   const int64_t tiles = ((g.M + 127) / 128) * ((g.N + kBlockN - 1) / kBlockN);
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
   kern<<<grid, 192, L::SMEM_BYTES, st>>>(tx, tg, tu, static_cast<int>(g.M), static_cast<int>(g.N),
-                                          static_cast<int>(g.K), kGroupM, idesc, ep, error_word_ptr());
+                                          static_cast<int>(g.K), kGroupM, idesc, ep, error_word_ptr(), 1);
   note_launch();
   return cudaGetLastError();
 }

@@ -79,13 +79,24 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 
 // Epi must provide:
 //   struct Params;
-//   __device__ void operator()(const Params&, const uint32_t (&acc)[NUM_B][16], int row, int col0, int M, int N)
+//   __device__ void operator()(const Params&, const uint32_t (&acc)[NUM_B][16], int row, int col0, int M, int N,
+//                              int split)
 //   called once per 16 accumulator columns per row (row < M not guaranteed).
-template <MmaKind KIND, int BLOCK_N, int NUM_B, int STAGES, class Epi>
+//
+// B_MN: the B operand is MN-major (B given as [K, N] with N contiguous, as
+// the reference's fp8_gemm passes it); each stage then holds BLOCK_N / 128
+// boxes of [128 K rows x 128 bytes of N], chained by the descriptor's
+// leading-byte offset. Only for 8-bit operands and NUM_B == 1.
+//
+// k_splits > 1 splits the K loop: work item w covers tile w / k_splits and
+// the K blocks of slice w % k_splits; the epilogue receives the slice index.
+template <MmaKind KIND, int BLOCK_N, int NUM_B, int STAGES, class Epi, bool B_MN = false>
 __global__ void __launch_bounds__(192, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
                      const __grid_constant__ CUtensorMap tmap_b1, int M, int N, int K, int group_m, uint32_t idesc,
-                     const typename Epi::Params ep, uint32_t* err) {
+                     const typename Epi::Params ep, uint32_t* err, int k_splits) {
+  static_assert(!B_MN || (NUM_B == 1 && KindTraits<KIND>::ELEM == 1 && BLOCK_N % 128 == 0),
+                "MN-major B: 8-bit operands, one B operand, BLOCK_N a multiple of 128");
   using L = GemmLayout<BLOCK_N, NUM_B, STAGES>;
   constexpr int KB_ELEMS = 128 / KindTraits<KIND>::ELEM;
 
@@ -104,6 +115,21 @@ __global__ void __launch_bounds__(192, 1)
   TileSched sched{(M + L::BM - 1) / L::BM, (N + BLOCK_N - 1) / BLOCK_N, group_m};
   const int num_tiles = sched.num_tiles();
   const int num_k = (K + KB_ELEMS - 1) / KB_ELEMS;
+  const int num_work = num_tiles * k_splits;
+  const int kb_per_split = (num_k + k_splits - 1) / k_splits;
+  // work item -> (tile, K-block range, slice)
+  struct Work {
+    int m_blk, n_blk, kb0, kb1, split;
+  };
+  auto work = [&](int w) {
+    Work r;
+    const int tile = w / k_splits;
+    r.split = w - tile * k_splits;
+    sched.coords(tile, r.m_blk, r.n_blk);
+    r.kb0 = r.split * kb_per_split;
+    r.kb1 = min(num_k, r.kb0 + kb_per_split);
+    return r;
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -133,18 +159,25 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int it = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
-        int m_blk, n_blk;
-        sched.coords(tile, m_blk, n_blk);
-        for (int kb = 0; kb < num_k; ++kb, ++it) {
+      for (int w = blockIdx.x; w < num_work && !*abort_flag; w += gridDim.x) {
+        const Work wk = work(w);
+        const int m_blk = wk.m_blk, n_blk = wk.n_blk;
+        for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!wait_or_abort(&empty[s], ph ^ 1, abort_flag, err, ERR_WAIT_TIMEOUT_PRODUCER)) break;
           mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
           const int kx = kb * KB_ELEMS;
           tma_load_2d(sa + s * L::A_BYTES, &tmap_a, &full[s], kx, m_blk * L::BM);
-          tma_load_2d(sb + (s * NUM_B) * L::B_BYTES, &tmap_b0, &full[s], kx, n_blk * BLOCK_N);
-          if constexpr (NUM_B == 2) tma_load_2d(sb + (s * NUM_B + 1) * L::B_BYTES, &tmap_b1, &full[s], kx, n_blk * BLOCK_N);
+          if constexpr (B_MN) {
+#pragma unroll
+            for (int c = 0; c < BLOCK_N / 128; ++c)
+              tma_load_2d(sb + s * L::B_BYTES + c * (128 * 128), &tmap_b0, &full[s], n_blk * BLOCK_N + c * 128, kx);
+          } else {
+            tma_load_2d(sb + (s * NUM_B) * L::B_BYTES, &tmap_b0, &full[s], kx, n_blk * BLOCK_N);
+            if constexpr (NUM_B == 2)
+              tma_load_2d(sb + (s * NUM_B + 1) * L::B_BYTES, &tmap_b1, &full[s], kx, n_blk * BLOCK_N);
+          }
         }
       }
     }
@@ -152,14 +185,16 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       int it = 0, tcount = 0;
-      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++tcount) {
+      for (int w = blockIdx.x; w < num_work && !*abort_flag; w += gridDim.x, ++tcount) {
+        const Work wk = work(w);
+        const int kb0 = wk.kb0, kb1 = wk.kb1;
         const int acc = tcount & 1;
         const uint32_t aph = (tcount >> 1) & 1;
         if (!wait_or_abort(&tempty[acc], aph ^ 1, abort_flag, err, ERR_WAIT_TIMEOUT_MMA)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * L::ACC_COLS;
         bool ok = true;
-        for (int kb = 0; kb < num_k; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!wait_or_abort(&full[s], ph, abort_flag, err, ERR_WAIT_TIMEOUT_MMA)) { ok = false; break; }
@@ -173,8 +208,10 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t adesc = smem_desc_kmajor_sw128(a_addr + kk * 32);
-            const uint64_t bdesc = smem_desc_kmajor_sw128(b_addr + kk * 32);
-            umma<KIND>(d_tmem, adesc, bdesc, idesc, (kb | kk) != 0 ? 1u : 0u);
+            // MN-major B: 32 K rows of 128 bytes per instruction = 4 swizzle atoms
+            const uint64_t bdesc = B_MN ? smem_desc_mnmajor_sw128(b_addr + kk * 4096, 128 * 128)
+                                        : smem_desc_kmajor_sw128(b_addr + kk * 32);
+            umma<KIND>(d_tmem, adesc, bdesc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
           }
           umma_commit(&empty[s]);
         }
@@ -188,13 +225,13 @@ __global__ void __launch_bounds__(192, 1)
     const int row_in_tile = sub * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
     int tcount = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++tcount) {
+    for (int w = blockIdx.x; w < num_work; w += gridDim.x, ++tcount) {
       const int acc = tcount & 1;
       const uint32_t aph = (tcount >> 1) & 1;
       if (!wait_or_abort(&tfull[acc], aph, abort_flag, err, ERR_WAIT_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
-      int m_blk, n_blk;
-      sched.coords(tile, m_blk, n_blk);
+      const Work wk = work(w);
+      const int m_blk = wk.m_blk, n_blk = wk.n_blk, split = wk.split;
       const int row = m_blk * L::BM + row_in_tile;
       const uint32_t base = tmem_base + lane_addr + acc * L::ACC_COLS;
 #pragma unroll 1
@@ -203,7 +240,7 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N + c, r[j]);
         tmem_ld_wait();
-        Epi{}(ep, r, row, n_blk * BLOCK_N + c, M, N);
+        Epi{}(ep, r, row, n_blk * BLOCK_N + c, M, N, split);
       }
       tc_fence_before();
       __syncwarp();
