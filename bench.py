@@ -266,9 +266,65 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # GPU step
 # ---------------------------------------------------------------------------
+def time_graph(calls, reps: int = 20):
+    """Device-side microseconds per call.
+
+    `calls` hold one call per rotating input set (together larger than L2, so
+    each call finds its inputs in HBM). They are captured once into a CUDA
+    graph, which is replayed `reps` times between two CUDA events; host work
+    per call (Python, validation, ctypes) is outside the measurement.
+    Returns (us, None) or (None, error text) if the capture failed.
+    """
+    import torch
+
+    for c in calls:
+        c()  # lazy module loading, workspace sizing
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for c in calls:
+            c()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(g):
+            for c in calls:
+                c()
+    except Exception as exc:  # noqa: BLE001 - reported in the JSON line
+        torch.cuda.synchronize()
+        return None, f"{type(exc).__name__}: {exc}"[:200]
+    g.replay()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(reps):
+        g.replay()
+    b.record()
+    b.synchronize()
+    us = a.elapsed_time(b) * 1e3 / (reps * len(calls))
+    del g
+    torch.cuda.synchronize()
+    return us, None
+
+
+def _copies(make, nbytes_each: int, min_total: int = 2 * L2_BYTES, cap: int = 128):
+    """Enough independent tensors from make() that together they exceed min_total bytes."""
+    n = max(2, min(cap, -(-min_total // max(1, nbytes_each))))
+    return [make() for _ in range(n)]
+
+
 def components(peaks, flush_buf):
-    """Per-op kernel numbers at the other configurations (rank 0)."""
-    import numpy as np
+    """Per-op numbers at the other configurations (rank 0).
+
+    For each op: ``us`` = device time per call from CUDA-graph replay over
+    rotating inputs larger than L2 (the kernel-side number the roofline
+    fraction uses), ``us_call`` = one call through the Python API timed alone
+    with CUDA events after an L2 flush (includes host overhead and launch
+    latency).
+    """
     import torch
 
     import triton_ops
@@ -276,43 +332,102 @@ def components(peaks, flush_buf):
     out = {}
     dev = torch.device("cuda")
     g = torch.Generator(device="cuda").manual_seed(5)
-    # RMSNorm+RoPE at [2, 128, 4096] (launch-latency bound; fits in L2)
-    x = torch.randn(2, 128, 4096, device=dev, dtype=torch.float16, generator=g)
+    hbm = peaks["hbm_gbs"]
+
+    def entry(us, err, us_call, nbytes=None, flops=None, peak=None):
+        e = {"us": us, "us_call": us_call}
+        if err:
+            e["graph_error"] = err
+        t = us if us is not None else us_call
+        if nbytes is not None:
+            e["GB/s"] = nbytes / t / 1e3
+            e["frac_hbm"] = nbytes / t / 1e3 / hbm
+        if flops is not None:
+            e["TFLOP/s"] = flops / t / 1e6
+            if peak is not None:
+                e["frac_peak"] = flops / t / 1e6 / peak
+        return e
+
+    # RMSNorm+RoPE at [2, 128, 4096] (launch-latency bound)
+    def mk_x():
+        return torch.randn(2, 128, 4096, device=dev, dtype=torch.float16, generator=g)
+    xs = _copies(mk_x, 2 * 128 * 4096 * 2)
     w = (1 + 0.1 * torch.randn(4096, device=dev, generator=g)).half()
     cos, sin = rope_tables(128, 64, dev)
-    ms = time_events(lambda: triton_ops.fused_rmsnorm_rope(x, w, cos, sin), 50, flush_buf)
     nbytes = 2 * (2 * 128 * 4096 * 2) + 4096 * 2 + 2 * (128 * 32 * 2)
-    out["rmsnorm_rope_2x128x4096"] = {"us": ms * 1e3, "GB/s": nbytes / ms / 1e6}
-    # FP8 quantize / dequantize at [4096, 4096] with 0.1% outliers
-    t = torch.randn(4096, 4096, device=dev, generator=g).half()
-    idx = torch.randperm(t.numel(), device=dev, generator=g)[: t.numel() // 1000]
-    t.view(-1)[idx] = 200.0 * torch.sign(torch.randn(idx.numel(), device=dev, generator=g)).half()
-    q, s = triton_ops.quantize_fp8(t)
-    ms_q = time_events(lambda: triton_ops.quantize_fp8(t), 30, flush_buf)
-    ms_d = time_events(lambda: triton_ops.dequantize_fp8(q, s), 30, flush_buf)
-    nb = 3 * t.numel()
-    out["fp8_quantize_4096x4096"] = {"us": ms_q * 1e3, "GB/s": nb / ms_q / 1e6, "frac_hbm": nb / ms_q / 1e6 / peaks["hbm_gbs"]}
-    out["fp8_dequantize_4096x4096"] = {"us": ms_d * 1e3, "GB/s": nb / ms_d / 1e6, "frac_hbm": nb / ms_d / 1e6 / peaks["hbm_gbs"]}
-    # FP8 GEMM over M (reference codec, int8 tensor cores), N = K = 4096
-    b = torch.randn(4096, 4096, device=dev, generator=g).half()
-    qb, sb = triton_ops.quantize_fp8(b)
-    gemm = {}
+    us, err = time_graph([lambda x=x: triton_ops.fused_rmsnorm_rope(x, w, cos, sin) for x in xs])
+    us_call = 1e3 * time_events(lambda: triton_ops.fused_rmsnorm_rope(xs[0], w, cos, sin), 50, flush_buf)
+    out["rmsnorm_rope_2x128x4096"] = entry(us, err, us_call, nbytes=nbytes)
+    del xs
+
+    # FP8 quantize / dequantize at [4096, 4096] fp16 with 0.1% outliers of +-200
+    def mk_t():
+        t = torch.randn(4096, 4096, device=dev, generator=g).half()
+        idx = torch.randperm(t.numel(), device=dev, generator=g)[: t.numel() // 1000]
+        t.view(-1)[idx] = 200.0 * torch.sign(torch.randn(idx.numel(), device=dev, generator=g)).half()
+        return t
+    ts = _copies(mk_t, 4096 * 4096 * 2)
+    nb = 3 * 4096 * 4096
+    for name, qd in (("", torch.uint8), ("_e4m3", torch.float8_e4m3fn)):
+        us, err = time_graph([lambda t=t: triton_ops.quantize_fp8(t, dtype=qd) for t in ts])
+        us_call = 1e3 * time_events(lambda: triton_ops.quantize_fp8(ts[0], dtype=qd), 30, flush_buf)
+        out[f"fp8_quantize{name}_4096x4096"] = entry(us, err, us_call, nbytes=nb)
+        qs = [triton_ops.quantize_fp8(t, dtype=qd) for t in ts]
+        us, err = time_graph([lambda q=q, s=s: triton_ops.dequantize_fp8(q, s) for q, s in qs])
+        us_call = 1e3 * time_events(lambda: triton_ops.dequantize_fp8(*qs[0]), 30, flush_buf)
+        out[f"fp8_dequantize{name}_4096x4096"] = entry(us, err, us_call, nbytes=nb)
+        del qs
+    del ts
+
+    # FP8 GEMM over M, N = K = 4096: reference codec (int8 tensor cores), e4m3
+    # (fp8 tensor cores), and the library fp8 GEMM (torch._scaled_mm) on the
+    # same e4m3 operands as a comparator
+    def mk_b():
+        return torch.randn(4096, 4096, device=dev, generator=g).half()
+    bs = [triton_ops.quantize_fp8(b, dtype=torch.uint8) for b in _copies(mk_b, 4096 * 4096, cap=16)]
+    bs8 = [triton_ops.quantize_fp8(b, dtype=torch.float8_e4m3fn) for b in _copies(mk_b, 4096 * 4096, cap=16)]
+    bs8_nk = [(q.t().contiguous(), s) for q, s in bs8]
+    gemm, gemm8, lib8 = {}, {}, {}
     for M in (16, 128, 1024, 4096, 8192):
-        a = torch.randn(M, 4096, device=dev, generator=g).half()
-        qa, sa = triton_ops.quantize_fp8(a)
-        ms = time_events(lambda: triton_ops.fp8_gemm(qa, qb, sa, sb), 20, flush_buf)
         fl = 2.0 * M * 4096 * 4096
-        gemm[str(M)] = {"us": ms * 1e3, "TFLOP/s": fl / ms / 1e9}
-    out["fp8_gemm_Nx4096x4096"] = gemm
-    # gated MLP at [2, 1024, 4096] x [11264, 4096], SiLU and tanh-GELU
-    xm = torch.randn(2, 1024, 4096, device=dev, generator=g).half()
+        def mk_a():
+            return torch.randn(M, 4096, device=dev, generator=g).half()
+        a_f = _copies(mk_a, M * 4096, cap=len(bs))
+        a_f = (a_f * ((len(bs) + len(a_f) - 1) // len(a_f)))[: len(bs)]
+        qa = [triton_ops.quantize_fp8(a, dtype=torch.uint8) for a in a_f]
+        qa8 = [triton_ops.quantize_fp8(a, dtype=torch.float8_e4m3fn) for a in a_f]
+        pairs = list(zip(qa, bs))
+        us, err = time_graph([lambda a=a, b=b: triton_ops.fp8_gemm(a[0], b[0], a[1], b[1]) for a, b in pairs])
+        us_call = 1e3 * time_events(lambda: triton_ops.fp8_gemm(qa[0][0], bs[0][0], qa[0][1], bs[0][1]), 20, flush_buf)
+        gemm[str(M)] = entry(us, err, us_call, flops=fl)
+        pairs8 = list(zip(qa8, bs8))
+        us, err = time_graph([lambda a=a, b=b: triton_ops.fp8_gemm(a[0], b[0], a[1], b[1]) for a, b in pairs8])
+        us_call = 1e3 * time_events(lambda: triton_ops.fp8_gemm(qa8[0][0], bs8[0][0], qa8[0][1], bs8[0][1]), 20,
+                                    flush_buf)
+        gemm8[str(M)] = entry(us, err, us_call, flops=fl)
+        try:
+            one = torch.ones((), device=dev)
+            libs = [lambda a=a, b=b: torch._scaled_mm(a[0], b[0].t(), one, one, out_dtype=torch.float16)
+                    for a, b in zip(qa8, bs8_nk)]
+            us, err = time_graph(libs)
+            lib8[str(M)] = entry(us, err, None, flops=fl)
+        except Exception as exc:  # noqa: BLE001 - comparator only
+            lib8[str(M)] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
+        del qa, qa8, a_f
+    out["fp8_gemm_Mx4096x4096"] = gemm
+    out["fp8_gemm_e4m3_Mx4096x4096"] = gemm8
+    out["library_scaled_mm_e4m3_Mx4096x4096"] = lib8
+    del bs, bs8, bs8_nk
+
+    # gated MLP at [2, 1024, 4096] x [11264, 4096] (weights alone exceed L2)
+    xm = [torch.randn(2, 1024, 4096, device=dev, generator=g).half() for _ in range(2)]
     wg = (0.02 * torch.randn(11264, 4096, device=dev, generator=g)).half()
     wu = (0.02 * torch.randn(11264, 4096, device=dev, generator=g)).half()
+    fl = 4.0 * 2048 * 11264 * 4096
     for act in ("silu", "gelu_tanh"):
-        ms = time_events(lambda: triton_ops.fused_gated_mlp(xm, wg, wu, act), 20, flush_buf)
-        fl = 4.0 * 2048 * 11264 * 4096
-        out[f"gated_mlp_2x1024x4096_{act}"] = {"us": ms * 1e3, "TFLOP/s": fl / ms / 1e9,
-                                                "frac_tensor_burst": fl / ms / 1e9 / peaks["bf16_tflops"]}
+        us, err = time_graph([lambda x=x: triton_ops.fused_gated_mlp(x, wg, wu, act) for x in xm], reps=10)
+        us_call = 1e3 * time_events(lambda: triton_ops.fused_gated_mlp(xm[0], wg, wu, act), 20, flush_buf)
+        out[f"gated_mlp_2x1024x4096_{act}"] = entry(us, err, us_call, flops=fl, peak=peaks["bf16_tflops"])
     return out
 
 

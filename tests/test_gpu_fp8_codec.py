@@ -196,3 +196,54 @@ def test_e4m3_all_fp16_patterns_vs_torch_cast(cuda):
     assert torch.equal(q.view(torch.uint8), ref.view(torch.uint8))
     d = dequantize_fp8(q, s, torch.float32)
     assert torch.equal(d, ref.float() / s)
+
+
+@pytest.mark.parametrize("amax", [448.0, 200.0, 1.0, 3.7e-3, 65504.0, 1.0e-30])
+def test_dynamic_scale_threshold_neighbourhoods(cuda, amax):
+    """Dynamic-scale quantize (the in-range fast encode) at every code boundary, bit-exact."""
+    from triton_ops import quantize_fp8
+
+    s = O.compute_scale(np.array([amax], np.float32))
+    centres = np.array([(k + 0.5) * 448.0 / 127.0 for k in range(-128, 128)], np.float64) / float(s)
+    bits = centres.astype(np.float32).view(np.int32)[:, None] + np.arange(-48, 49, dtype=np.int32)[None, :]
+    vals = bits.view(np.float32).ravel()
+    vals = vals[np.isfinite(vals) & (np.abs(vals) <= np.float32(amax))]
+    vals = np.concatenate([np.array([amax, -amax, 0.0, -0.0], np.float32), vals]).astype(np.float32)
+    for dt in ("f32", "f16", "bf16"):
+        x = O.round_to(vals, dt)
+        if not np.isfinite(x).all() or np.abs(x).max() == 0:
+            continue
+        q, sc = quantize_fp8(dev_tensor(x, dt))
+        s_ref = O.compute_scale(x)
+        assert f32bits(sc.item()) == f32bits(s_ref)
+        np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(x, s_ref))
+
+
+def test_dynamic_scale_all_finite_fp16(cuda):
+    """Every finite fp16 value under its own dynamic scale (448 / 65504), both encodings."""
+    from triton_ops import quantize_fp8
+
+    allh = np.arange(65536, dtype=np.uint16).view(np.float16)
+    xh = allh[np.isfinite(allh)].astype(np.float32)
+    x = torch.from_numpy(xh.astype(np.float16)).cuda()
+    q, s = quantize_fp8(x)
+    s_ref = O.compute_scale(xh)
+    assert f32bits(s.item()) == f32bits(s_ref)
+    np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(xh, s_ref))
+    q8, s8 = quantize_fp8(x, dtype=torch.float8_e4m3fn)
+    ref = (x.float() * s8).clamp(-448, 448).to(torch.float8_e4m3fn)
+    assert torch.equal(q8.view(torch.uint8), ref.view(torch.uint8))
+
+
+def test_dynamic_scale_nan_and_inf_inputs(cuda):
+    """amax NaN (scale NaN) and amax inf (scale 0) take the careful encode: codes match the oracle."""
+    from triton_ops import quantize_fp8
+
+    rng = np.random.default_rng(3)
+    for bad in (np.nan, np.inf, -np.inf):
+        x = rng.standard_normal(4099).astype(np.float32)
+        x[17] = bad
+        q, s = quantize_fp8(torch.from_numpy(x).cuda())
+        s_ref = O.compute_scale(x)
+        assert f32bits(s.item()) == f32bits(s_ref)
+        np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(x, s_ref))

@@ -174,3 +174,64 @@ def test_validation(cuda):
         fp8_gemm(a, torch.zeros(16, 8, dtype=torch.uint8, device="cuda"), s, s, torch.int32)
     with pytest.raises(UnsupportedDtypeError):
         fp8_gemm(a, torch.zeros(16, 8, dtype=torch.float8_e4m3fn, device="cuda"), s, s)
+
+
+# Shapes whose 128 x 256 tiles fill the GPU use two-CTA 256 x 256 tiles; ragged
+# M leaves the second CTA's rows partly or wholly outside the matrix.
+@pytest.mark.parametrize("M,N,K", [(300, 12800, 256), (1000, 4864, 384), (129, 37888, 128), (4095, 4096, 200)])
+def test_pair_tiles_ragged(cuda, M, N, K):
+    from triton_ops import fp8_gemm
+
+    qa, sa = codes(M, K, M + 3)
+    qb, sb = codes(K, N, N + 4)
+    out = fp8_gemm(qa, qb, sa, sb, torch.float32)
+    rows = torch.cat([torch.arange(0, min(M, 40)), torch.arange(max(0, M - 40), M)]).unique()
+    ref = O.fp8_gemm(qa[rows.cuda()].cpu().numpy(), qb.cpu().numpy(), sa.item(), sb.item(), "f32")
+    assert O.rel_fro(host(out[rows.cuda()]), ref) <= 1e-5
+
+
+def test_pair_tiles_e4m3_and_nk_layout(cuda):
+    from triton_ops import FP8Linear, fp8_gemm, quantize_fp8
+
+    g = torch.Generator(device="cuda").manual_seed(7)
+    a = torch.randn(520, 512, device="cuda", generator=g).half()
+    b = torch.randn(512, 9472, device="cuda", generator=g).half()
+    qa, sa = quantize_fp8(a, dtype=torch.float8_e4m3fn)
+    qb, sb = quantize_fp8(b, dtype=torch.float8_e4m3fn)
+    out = host(fp8_gemm(qa, qb, sa, sb, torch.float32))
+    ref = (qa.float() / sa) @ (qb.float() / sb)
+    assert O.rel_fro(out, host(ref)) <= 1e-5
+    lin = FP8Linear(512, 9472).cuda()
+    x = torch.randn(600, 512, device="cuda", generator=g)
+    y = host(lin(x))
+    xq, xs = quantize_fp8(x)
+    ref = O.fp8_gemm(xq.cpu().numpy(), lin.weight_fp8.cpu().numpy().T.copy(), xs.item(), lin.weight_scale.item(), "f32")
+    assert O.rel_fro(y, ref) <= 1e-5
+
+
+def test_pair_and_single_cta_tiles_agree(cuda, tmp_path):
+    """The same problem with two-CTA tiles switched off (TFO_B200_PAIR_MMA=0) gives identical bytes."""
+    import os
+    import subprocess
+    import sys
+
+    from conftest import PKG, ROOT
+    from triton_ops import fp8_gemm
+
+    qa, sa = codes(1000, 384, 11)
+    qb, sb = codes(384, 4864, 12)
+    np.save(tmp_path / "qa.npy", qa.cpu().numpy())
+    np.save(tmp_path / "qb.npy", qb.cpu().numpy())
+    prog = (
+        "import sys, numpy as np, torch; sys.path[:0] = [%r, %r]\n"
+        "from triton_ops import fp8_gemm\n"
+        "qa = torch.from_numpy(np.load(%r)).cuda(); qb = torch.from_numpy(np.load(%r)).cuda()\n"
+        "o = fp8_gemm(qa, qb, torch.tensor(%r, device='cuda'), torch.tensor(%r, device='cuda'), torch.float16)\n"
+        "np.save(%r, o.cpu().numpy())\n"
+    ) % (str(PKG), str(ROOT), str(tmp_path / "qa.npy"), str(tmp_path / "qb.npy"), sa.item(), sb.item(),
+         str(tmp_path / "single.npy"))
+    env = dict(os.environ, TFO_B200_PAIR_MMA="0")
+    subprocess.run([sys.executable, "-c", prog], check=True, env=env, timeout=300)
+    single = np.load(tmp_path / "single.npy")
+    pair = fp8_gemm(qa, qb, sa, sb, torch.float16).cpu().numpy()
+    np.testing.assert_array_equal(pair.view(np.uint16), single.view(np.uint16))

@@ -117,3 +117,21 @@ def test_validation(cuda):
         fused_gated_mlp(x, w, w, "relu")
     with pytest.raises(ShapeMismatchError):
         fused_gated_mlp(x, w, w[:, :128].contiguous())
+
+
+# Two-CTA tiles (M > 128): ragged M, both 16-bit dtypes and the tf32 path.
+@pytest.mark.parametrize("M,N,K,xd,wd,act", [
+    (300, 1000, 640, "f16", "f16", "silu"),
+    (2000, 640, 4096, "bf16", "bf16", "gelu"),
+    (257, 384, 512, "f16", "f16", "gelu_tanh"),
+    (200, 96, 256, "f16", "f32", "silu"),
+])
+def test_pair_tiles(cuda, M, N, K, xd, wd, act):
+    from triton_ops import fused_gated_mlp
+
+    x, wg, wu = mlp_inputs(M, N, K, xd, wd, wstd=0.1, seed=M + 2 * N + K)
+    out = host(fused_gated_mlp(x.view(1, M, K), wg, wu, act))[0]
+    rows = np.unique(np.r_[0:min(M, 64), max(0, M - 64):M])
+    ref = O.gated_mlp(host(x)[rows], host(wg), host(wu), act, xd)
+    tf32 = "f32" in (xd, wd)
+    assert O.rel_fro(out[rows], ref) <= (TOL if tf32 else 3e-3)

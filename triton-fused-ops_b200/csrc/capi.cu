@@ -1,6 +1,8 @@
 // C-ABI layer: argument checks, status/error reporting, device caches and
 // dispatch into the kernel translation units.
+#include <algorithm>
 #include <atomic>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 #include <tuple>
@@ -80,8 +82,51 @@ int cached_occupancy(const void* kernel, int block, size_t smem) {
   return occ;
 }
 
+bool pair_mma_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("TFO_B200_PAIR_MMA");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
+
+int gemm_resident_units(const void* kernel, size_t smem, int cg) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, size_t, int, int>, int> cache;
+  const auto key = std::make_tuple(kernel, smem, cg, dev);
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) != cudaSuccess)
+    return 0;
+  int units = 0;
+  if (cg == 1) {
+    int occ = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, 192, smem) != cudaSuccess) return 0;
+    units = occ * num_sms();
+  } else {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * num_sms());
+    cfg.blockDim = dim3(192);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&units, kernel, &cfg) != cudaSuccess) return 0;
+  }
+  cache[key] = units;
+  return units;
+}
+
 size_t scale_workspace_bytes(int64_t numel) {
-  return static_cast<size_t>(amax_partials_count(numel)) * sizeof(uint32_t);
+  return std::max(static_cast<size_t>(amax_partials_count(numel)) * sizeof(uint32_t),
+                  quantize_dynamic_workspace_bytes());
 }
 
 // Waits on an mbarrier that nothing ever arrives on, with the given cycle
@@ -192,8 +237,9 @@ int tfo_fp8_quantize(const void* x, int64_t numel, int x_dtype, const float* sca
       return TFO_OK;
     }
     if (!x || !out) return fail(TFO_ERR_INVALID, "tfo_fp8_quantize: NULL pointer");
-    e = amax_partials_launch(x, numel, x_dtype, parts, nparts, st);
-    if (e == cudaSuccess) e = encode_launch(x, numel, x_dtype, nullptr, parts, nparts, scale_out, out, out_dtype, st);
+    if (workspace_bytes < quantize_dynamic_workspace_bytes())
+      return fail(TFO_ERR_INVALID, "tfo_fp8_quantize: workspace too small");
+    e = quantize_dynamic_launch(x, numel, x_dtype, scale_out, out, out_dtype, workspace, workspace_bytes, st);
   } else {
     if (numel == 0) return TFO_OK;
     if (!x || !out) return fail(TFO_ERR_INVALID, "tfo_fp8_quantize: NULL pointer");

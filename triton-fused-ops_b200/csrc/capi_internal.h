@@ -7,6 +7,7 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <utility>
 
 namespace tfo {
 
@@ -22,6 +23,37 @@ uint32_t* error_word_ptr();
 int num_sms();
 // cudaOccupancyMaxActiveBlocksPerMultiprocessor, cached per (kernel, block, smem).
 int cached_occupancy(const void* kernel, int block, size_t smem);
+// For a persistent GEMM kernel (192 threads, `smem` bytes of dynamic shared
+// memory, raised on first use): how many work units can be resident at once
+// on the current device, a unit being one CTA (cg == 1) or one cluster of two
+// CTAs (cg == 2). Cached per (kernel, smem, cg, device); 0 on error.
+int gemm_resident_units(const void* kernel, size_t smem, int cg);
+
+// Two-CTA (cta_group::2) GEMM tiles are used where they apply unless the
+// environment sets TFO_B200_PAIR_MMA=0 (read once per process).
+bool pair_mma_enabled();
+
+// Launches a persistent GEMM kernel: `units` work units (see above) of 192
+// threads, as clusters of two CTAs when cg == 2.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_gemm_units(void (*kernel)(KArgs...), int cg, int units, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(units * cg));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (cg == 2) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = (cg == 2) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 struct RmsNormRopeArgs {
   const void* x;
@@ -47,6 +79,12 @@ cudaError_t encode_launch(const void* x, int64_t n, int x_dtype, const float* sc
                           int nparts, float* scale_out, void* out, int out_dtype, cudaStream_t st);
 cudaError_t dequantize_launch(const void* q, int64_t n, int q_dtype, const float* scale, void* out, int out_dtype,
                               cudaStream_t st);
+// Workspace of the one-kernel dynamic-scale quantize: a barrier word at byte
+// 0 (zeroed by quantize_dynamic_launch) and one amax partial per CTA from
+// byte 256.
+size_t quantize_dynamic_workspace_bytes();
+cudaError_t quantize_dynamic_launch(const void* x, int64_t n, int x_dtype, float* scale_out, void* out, int out_dtype,
+                                    void* ws, size_t ws_bytes, cudaStream_t st);
 
 // FP8 GEMM (fp8_gemm.cu). b_layout: 0 = [K, N] row-major, 1 = [N, K] row-major.
 struct Fp8GemmArgs {

@@ -31,6 +31,7 @@ enum : uint32_t {
   ERR_WAIT_TIMEOUT_EPILOGUE = 1u << 2,
   ERR_WAIT_TIMEOUT_OTHER = 1u << 3,
   ERR_BAD_LAUNCH = 1u << 4,
+  ERR_GRID_BARRIER = 1u << 5,
 };
 
 // ~2^31 SM cycles (about a second at 1.9 GHz): far above any legitimate wait
@@ -221,6 +222,81 @@ __device__ __forceinline__ void umma(uint32_t d_tmem, uint64_t a_desc, uint64_t 
 // completed (their shared-memory operands may then be overwritten).
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// Two-CTA (cta_group::2) forms: a cluster of two CTAs on two SMs shares one
+// M = 256 MMA. Each CTA holds half of A (its 128 rows) and half of B (N / 2
+// rows) at the same shared-memory offsets; the even CTA of the pair issues the
+// MMA, and each CTA's TMEM receives its own 128 accumulator rows. No
+// multicast form of any instruction is used.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Full cluster barrier (all threads of both CTAs), release/acquire.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// Address of the same shared-memory variable in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+// Arrive (release, cluster scope) on an mbarrier given by its cluster address.
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t bar_cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar_cluster_addr) : "memory");
+}
+// 2-D tiled load into this CTA's shared memory whose transaction bytes are
+// reported to an mbarrier that may live in the peer CTA of the pair.
+__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const void* tmap, uint32_t bar_cluster_addr,
+                                                 int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+      "[%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar_cluster_addr), "r"(x), "r"(y)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t* smem_result, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(smem_result)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+template <MmaKind K>
+__device__ __forceinline__ void umma_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  const uint32_t z = 0;  // disable-output-lane mask (8 words for a pair): none disabled
+#define TFO_UMMA_PAIR(KSTR)                                                                                     \
+  asm volatile("{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"                                             \
+               "tcgen05.mma.cta_group::2.kind::" KSTR " [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" \
+               ::"r"(d_tmem), "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z))
+  if constexpr (K == MmaKind::F16) {
+    TFO_UMMA_PAIR("f16");
+  } else if constexpr (K == MmaKind::TF32) {
+    TFO_UMMA_PAIR("tf32");
+  } else if constexpr (K == MmaKind::I8) {
+    TFO_UMMA_PAIR("i8");
+  } else {
+    TFO_UMMA_PAIR("f8f6f4");
+  }
+#undef TFO_UMMA_PAIR
+}
+
+// Arrive on the mbarrier at cluster address `bar_cluster_addr` (this CTA's
+// or the peer's) once every pair MMA issued so far by this thread is done.
+__device__ __forceinline__ void umma_commit_pair(uint32_t bar_cluster_addr) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster_addr)
                : "memory");
 }
 

@@ -53,114 +53,189 @@ __device__ __forceinline__ uint32_t ref_encode(float c) {
   return static_cast<uint32_t>(k + 128) & 0xffu;
 }
 
-// ---- loading 16 elements as fp32 ------------------------------------------
-template <typename T> struct Load16;
-template <> struct Load16<__half> {
-  static constexpr int VECS = 2;  // 16-byte vectors per 16 elements
+// Reference-codec bytes of four scaled values with |c| <= 448 + 1 ulp (true
+// for every element under a finite, non-zero dynamic scale s = 448 / amax):
+// no clamp or NaN handling is needed, and rint(y) for |y| <= 128 is read
+// from the low byte of y + 1.5 * 2^23 (one round-to-nearest-even addition,
+// exact for |y| < 2^22). The low byte is rint(y) mod 256, so the code
+// rint(y) + 128 is that byte XOR 0x80.
+__device__ __forceinline__ uint32_t ref_encode4_in_range(float c0, float c1, float c2, float c3) {
+  auto kbits = [](float c) -> uint32_t {
+    constexpr float kInv7 = 0.142857142857142857f;
+    const float q0 = __fmul_rn(c, kInv7);
+    const float r = __fmaf_rn(-q0, 7.0f, c);
+    const float q = __fmaf_rn(r, kInv7, q0);
+    return __float_as_uint(__fadd_rn(__fmul_rn(q, 1.984375f), 12582912.0f));
+  };
+  const uint32_t lo = __byte_perm(kbits(c0), kbits(c1), 0x0040);
+  const uint32_t hi = __byte_perm(kbits(c2), kbits(c3), 0x0040);
+  return __byte_perm(lo, hi, 0x5410) ^ 0x80808080u;
+}
+
+// ---- 16 elements at a time -------------------------------------------------
+// A chunk is 16 consecutive elements: two 16-byte vectors for 16-bit types,
+// four for fp32. Loads are issued for several chunks before any of them is
+// used, so each thread keeps that many vectors in flight.
+template <typename T> struct Chunk {
+  static constexpr int VECS = 16 * static_cast<int>(sizeof(T)) / 16;
+  uint4 v[VECS];
   template <bool STREAM>
-  __device__ static void go(const __half* p, float (&f)[16]) {
+  __device__ __forceinline__ void load(const T* p) {
     const uint4* q = reinterpret_cast<const uint4*>(p);
 #pragma unroll
-    for (int v = 0; v < 2; ++v) {
-      uint4 u = STREAM ? __ldcs(q + v) : __ldg(q + v);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float2 p2 = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
-        f[v * 8 + 2 * i] = p2.x;
-        f[v * 8 + 2 * i + 1] = p2.y;
-      }
-    }
+    for (int i = 0; i < VECS; ++i) v[i] = STREAM ? __ldcs(q + i) : __ldg(q + i);
   }
-};
-template <> struct Load16<__nv_bfloat16> {
-  static constexpr int VECS = 2;
-  template <bool STREAM>
-  __device__ static void go(const __nv_bfloat16* p, float (&f)[16]) {
-    const uint4* q = reinterpret_cast<const uint4*>(p);
+  __device__ __forceinline__ void zero() {
 #pragma unroll
-    for (int v = 0; v < 2; ++v) {
-      uint4 u = STREAM ? __ldcs(q + v) : __ldg(q + v);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float2 p2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[i]));
-        f[v * 8 + 2 * i] = p2.x;
-        f[v * 8 + 2 * i + 1] = p2.y;
-      }
-    }
+    for (int i = 0; i < VECS; ++i) v[i] = make_uint4(0u, 0u, 0u, 0u);
   }
-};
-template <> struct Load16<float> {
-  static constexpr int VECS = 4;
-  template <bool STREAM>
-  __device__ static void go(const float* p, float (&f)[16]) {
-    const float4* q = reinterpret_cast<const float4*>(p);
+  __device__ __forceinline__ void to_f(float (&f)[16]) const {
 #pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      float4 u = STREAM ? __ldcs(q + v) : __ldg(q + v);
-      f[4 * v] = u.x; f[4 * v + 1] = u.y; f[4 * v + 2] = u.z; f[4 * v + 3] = u.w;
+    for (int i = 0; i < VECS; ++i) {
+      const uint32_t w[4] = {v[i].x, v[i].y, v[i].z, v[i].w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if constexpr (std::is_same<T, float>::value) {
+          f[4 * i + j] = __uint_as_float(w[j]);
+        } else if constexpr (std::is_same<T, __half>::value) {
+          const float2 p2 = __half22float2(*reinterpret_cast<const __half2*>(&w[j]));
+          f[8 * i + 2 * j] = p2.x;
+          f[8 * i + 2 * j + 1] = p2.y;
+        } else {
+          const float2 p2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+          f[8 * i + 2 * j] = p2.x;
+          f[8 * i + 2 * j + 1] = p2.y;
+        }
+      }
     }
   }
 };
 
-// ---- amax ------------------------------------------------------------------
+// max |x| over this thread's share of x, as the fp32 bit pattern (|x| >= 0
+// orders like its bits; NaN bits exceed every finite value, as in torch's max).
+// Chunk i belongs to thread i mod stride; U chunks are loaded per iteration.
+template <typename T, int U>
+__device__ __forceinline__ uint32_t amax_share(const T* __restrict__ x, int64_t n, bool vec, int64_t tid,
+                                               int64_t stride) {
+  uint32_t m = 0;
+  int64_t done = 0;
+  if (vec) {
+    const int64_t n16 = n / 16;
+    for (int64_t i = tid; i < n16; i += U * stride) {
+      Chunk<T> c[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (i + u * stride < n16) c[u].template load<false>(x + (i + u * stride) * 16);
+        else c[u].zero();
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        float f[16];
+        c[u].to_f(f);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) m = max(m, __float_as_uint(fabsf(f[j])));
+      }
+    }
+    done = n16 * 16;
+  }
+  for (int64_t i = done + tid; i < n; i += stride) m = max(m, __float_as_uint(fabsf(Ty<T>::to_f(x[i]))));
+  return m;
+}
+
+// Block-wide max of one value per thread; every thread gets the result.
+__device__ __forceinline__ uint32_t block_max_u32(uint32_t m, uint32_t* red /* smem, >= 32 */) {
+  m = warp_max_u32(m);
+  __syncthreads();  // red may still be read by an earlier call
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  uint32_t b = 0;
+  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) b = max(b, red[i]);
+  return b;
+}
+
+// The reference's host-side scale from amax (bits of a non-negative float):
+// fp32(448.0 / double(amax)), 1.0 for amax == 0.
+// A NaN amax gives the quiet NaN 0x7FC00000, the bits the reference's
+// Python float division produces.
+__device__ __forceinline__ float scale_from_amax(uint32_t amax_bits) {
+  const float amax = __uint_as_float(amax_bits);
+  if (amax != amax) return __uint_as_float(0x7FC00000u);
+  return (amax == 0.f) ? 1.0f : __double2float_rn(__ddiv_rn(448.0, static_cast<double>(amax)));
+}
+
+// Encodes this thread's share of x with scale s (chunk i -> thread i mod stride).
+// IN_RANGE: every |x * s| <= 448 + 1 ulp (a finite, non-zero dynamic scale).
+// For e4m3 the clamp to +-448 is the satfinite conversion itself (NaN stays
+// NaN, +-inf -> +-448), so both variants convert pairs directly.
+template <typename T, bool E4M3, int U, bool IN_RANGE>
+__device__ __forceinline__ void encode_share(const T* __restrict__ x, int64_t n, bool vec, float s,
+                                             uint8_t* __restrict__ out, int64_t tid, int64_t stride) {
+  auto enc1 = [s](float xf) -> uint32_t {
+    const float c = __fmul_rn(xf, s);
+    if constexpr (E4M3) {
+      return static_cast<uint32_t>(__nv_cvt_float_to_fp8(c, __NV_SATFINITE, __NV_E4M3));
+    } else {
+      return ref_encode(c);
+    }
+  };
+  auto enc4 = [s, &enc1](const float* f) -> uint32_t {
+    if constexpr (E4M3) {
+      const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(__fmul_rn(f[0], s), __fmul_rn(f[1], s)),
+                                                   __NV_SATFINITE, __NV_E4M3);
+      const uint32_t hi = __nv_cvt_float2_to_fp8x2(make_float2(__fmul_rn(f[2], s), __fmul_rn(f[3], s)),
+                                                   __NV_SATFINITE, __NV_E4M3);
+      return lo | (hi << 16);
+    } else if constexpr (IN_RANGE) {
+      return ref_encode4_in_range(__fmul_rn(f[0], s), __fmul_rn(f[1], s), __fmul_rn(f[2], s), __fmul_rn(f[3], s));
+    } else {
+      return enc1(f[0]) | (enc1(f[1]) << 8) | (enc1(f[2]) << 16) | (enc1(f[3]) << 24);
+    }
+  };
+  int64_t done = 0;
+  if (vec) {
+    const int64_t n16 = n / 16;
+    for (int64_t i = tid; i < n16; i += U * stride) {
+      Chunk<T> c[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (i + u * stride < n16) c[u].template load<true>(x + (i + u * stride) * 16);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (i + u * stride < n16) {
+          float f[16];
+          c[u].to_f(f);
+          uint32_t w[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) w[q] = enc4(f + 4 * q);
+          __stcs(reinterpret_cast<uint4*>(out) + i + u * stride, make_uint4(w[0], w[1], w[2], w[3]));
+        }
+      }
+    }
+    done = n16 * 16;
+  }
+  for (int64_t i = done + tid; i < n; i += stride) out[i] = static_cast<uint8_t>(enc1(Ty<T>::to_f(x[i])));
+}
+
+// ---- amax (scale-only calls and the no-allocation quantize) ----------------
 constexpr int kAmaxThreads = 256;
 
 template <typename T>
 __global__ void __launch_bounds__(kAmaxThreads) amax_partial_kernel(const T* __restrict__ x, int64_t n, bool vec,
                                                                      uint32_t* __restrict__ partials) {
-  uint32_t m = 0;
+  __shared__ uint32_t red[32];
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int64_t done = 0;
-  if (vec) {
-    const int64_t n16 = n / 16;
-    // four independent 16-element loads in flight per thread
-    for (int64_t i = tid; i < n16; i += 4 * stride) {
-      float f[4][16];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int64_t ii = i + u * stride;
-        if (ii < n16) {
-          Load16<T>::template go<false>(x + ii * 16, f[u]);
-        } else {
-#pragma unroll
-          for (int j = 0; j < 16; ++j) f[u][j] = 0.f;
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u)
-#pragma unroll
-        for (int j = 0; j < 16; ++j) m = max(m, __float_as_uint(fabsf(f[u][j])));
-    }
-    done = n16 * 16;
-  }
-  for (int64_t i = done + tid; i < n; i += stride) m = max(m, __float_as_uint(fabsf(Ty<T>::to_f(x[i]))));
-  m = warp_max_u32(m);
-  __shared__ uint32_t red[kAmaxThreads / 32];
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t b = 0;
-    for (int i = 0; i < kAmaxThreads / 32; ++i) b = max(b, red[i]);
-    partials[blockIdx.x] = b;
-  }
+  const uint32_t b = block_max_u32(amax_share<T, 4>(x, n, vec, tid, stride), red);
+  if (threadIdx.x == 0) partials[blockIdx.x] = b;
 }
 
-// Reduce the per-CTA partial maxima and derive the scale exactly as the
-// reference's host code does (double division, then rounding to fp32).
+// Reduces the per-CTA partial maxima (read through L2: other SMs wrote them)
+// and derives the scale exactly as the reference's host code does.
 __device__ __forceinline__ float reduce_partials_to_scale(const uint32_t* __restrict__ partials, int nparts,
-                                                          uint32_t* red /* smem, >= blockDim/32 */) {
+                                                          uint32_t* red /* smem, >= 32 */) {
   uint32_t m = 0;
-  for (int i = threadIdx.x; i < nparts; i += blockDim.x) m = max(m, partials[i]);
-  m = warp_max_u32(m);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
-  __syncthreads();
-  uint32_t b = 0;
-  for (int i = 0; i < static_cast<int>(blockDim.x >> 5); ++i) b = max(b, red[i]);
-  const float amax = __uint_as_float(b);
-  return (amax == 0.f) ? 1.0f : __double2float_rn(__ddiv_rn(448.0, static_cast<double>(amax)));
+  for (int i = threadIdx.x; i < nparts; i += blockDim.x) m = max(m, __ldcg(partials + i));
+  return scale_from_amax(block_max_u32(m, red));
 }
 
 __global__ void finalize_scale_kernel(const uint32_t* __restrict__ partials, int nparts, float* __restrict__ scale_out) {
@@ -169,7 +244,7 @@ __global__ void finalize_scale_kernel(const uint32_t* __restrict__ partials, int
   if (threadIdx.x == 0) *scale_out = s;
 }
 
-// ---- encode ----------------------------------------------------------------
+// ---- encode with a given scale, or from amax partials ----------------------
 constexpr int kEncThreads = 256;
 
 template <typename T, bool E4M3>
@@ -178,7 +253,7 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const T* __restrict
                                                              const uint32_t* __restrict__ partials, int nparts,
                                                              float* __restrict__ scale_out, uint8_t* __restrict__ out) {
   __shared__ float s_sh;
-  __shared__ uint32_t red[kEncThreads / 32];
+  __shared__ uint32_t red[32];
   if (partials != nullptr) {
     const float s = reduce_partials_to_scale(partials, nparts, red);
     if (threadIdx.x == 0) {
@@ -189,40 +264,75 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const T* __restrict
     s_sh = *scale_in;
   }
   __syncthreads();
-  const float s = s_sh;
-
-  auto enc1 = [&](float xf) -> uint32_t {
-    const float c = __fmul_rn(xf, s);
-    if constexpr (E4M3) {
-      const float cl = min_nan(max_nan(c, -448.0f), 448.0f);
-      return static_cast<uint32_t>(__nv_cvt_float_to_fp8(cl, __NV_SATFINITE, __NV_E4M3));
-    } else {
-      return ref_encode(c);
-    }
-  };
-
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  int64_t done = 0;
-  if (vec) {
-    const int64_t n16 = n / 16;
-    for (int64_t i = tid; i < n16; i += stride) {
-      float f[16];
-      Load16<T>::template go<true>(x + i * 16, f);
-      uint32_t w[4];
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        w[q] = enc1(f[4 * q]) | (enc1(f[4 * q + 1]) << 8) | (enc1(f[4 * q + 2]) << 16) | (enc1(f[4 * q + 3]) << 24);
+  const float s = s_sh;
+  if (partials != nullptr && s > 0.f && s < INFINITY) encode_share<T, E4M3, 2, true>(x, n, vec, s, out, tid, stride);
+  else encode_share<T, E4M3, 2, false>(x, n, vec, s, out, tid, stride);
+}
+
+// ---- dynamic-scale quantize in one kernel ----------------------------------
+// Cooperative launch (all CTAs resident). Pass 1: each CTA's max |x| goes to
+// partials[blockIdx]; CTAs then meet at a grid barrier, a counter in the
+// workspace that the host zeroes before the launch and every CTA increments
+// once. Pass 2: every CTA reduces the partials to the scale (CTA 0 publishes
+// it) and encodes the same elements it read in pass 1, which for tensors up
+// to the L2 size come back from L2 rather than HBM. The barrier wait is
+// bounded: on expiry the CTA sets ERR_GRID_BARRIER and returns without
+// writing its share of the output.
+constexpr int kQuantThreads = 512;
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <typename T, bool E4M3>
+__global__ void __launch_bounds__(kQuantThreads, 2)
+    quantize_dynamic_kernel(const T* __restrict__ x, int64_t n, bool vec, uint32_t* __restrict__ barrier,
+                            uint32_t* __restrict__ partials, float* __restrict__ scale_out,
+                            uint8_t* __restrict__ out, uint32_t* __restrict__ err) {
+  __shared__ uint32_t red[32];
+  __shared__ float s_sh;
+  __shared__ int ok_sh;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const uint32_t b = block_max_u32(amax_share<T, 4>(x, n, vec, tid, stride), red);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = b;
+    __threadfence();
+    atomicAdd(barrier, 1u);
+    int ok = 1;
+    if (ld_acquire_gpu(barrier) < gridDim.x) {
+      const long long t0 = clock64();
+      while (ld_acquire_gpu(barrier) < gridDim.x) {
+        if (clock64() - t0 > kWaitBudgetCycles) {
+          set_error(err, ERR_GRID_BARRIER);
+          ok = 0;
+          break;
+        }
+        __nanosleep(128);
       }
-      __stcs(reinterpret_cast<uint4*>(out) + i, make_uint4(w[0], w[1], w[2], w[3]));
     }
-    done = n16 * 16;
+    __threadfence();
+    ok_sh = ok;
   }
-  for (int64_t i = done + tid; i < n; i += stride) out[i] = static_cast<uint8_t>(enc1(Ty<T>::to_f(x[i])));
+  __syncthreads();
+  if (!ok_sh) return;
+  const float s = reduce_partials_to_scale(partials, gridDim.x, red);
+  if (threadIdx.x == 0) {
+    s_sh = s;
+    if (blockIdx.x == 0) *scale_out = s;
+  }
+  __syncthreads();
+  const float sc = s_sh;
+  if (sc > 0.f && sc < INFINITY) encode_share<T, E4M3, 2, true>(x, n, vec, sc, out, tid, stride);
+  else encode_share<T, E4M3, 2, false>(x, n, vec, sc, out, tid, stride);
 }
 
 // ---- decode ----------------------------------------------------------------
-constexpr int kDecThreads = 256;
+constexpr int kDecThreads = 512;
 
 // out = RN_out( dec(u) / s ), dec(u) = RN(RN(float(u - 128) / 127) * 448) for
 // the reference codec (triton_ops/kernels/fp8_quantize.py:305-312) or the
@@ -245,6 +355,7 @@ template <typename TO, bool E4M3>
 __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __restrict__ q, int64_t n, bool vec,
                                                              const float* __restrict__ scale, TO* __restrict__ out) {
   using R = typename Raw<TO>::type;
+  constexpr int U = 4;  // 16-byte code vectors in flight per thread
   // One copy of the 256 outputs per lane (lut[u * 32 + lane]), so the
   // data-dependent lookups of a warp never collide on a shared-memory bank.
   __shared__ R base[256];
@@ -266,28 +377,36 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __re
   const uint32_t* my_lut = lut + (threadIdx.x & 31);
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  constexpr int OV = 16 * sizeof(R) / 16;  // 16-byte output vectors per code vector
   int64_t done = 0;
   if (vec) {
     const int64_t n16 = n / 16;
-    for (int64_t i = tid; i < n16; i += stride) {
-      const uint4 u = __ldcs(reinterpret_cast<const uint4*>(q) + i);
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-      uint32_t o[16 * sizeof(R) / 4];
-      if constexpr (sizeof(R) == 2) {
+    for (int64_t i = tid; i < n16; i += U * stride) {
+      uint4 in[U];
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t b0 = (w[k >> 1] >> (16 * (k & 1))) & 0xffu;
-          const uint32_t b1 = (w[k >> 1] >> (16 * (k & 1) + 8)) & 0xffu;
-          o[k] = my_lut[b0 * 32] | (my_lut[b1 * 32] << 16);
+      for (int u = 0; u < U; ++u)
+        if (i + u * stride < n16) in[u] = __ldcs(reinterpret_cast<const uint4*>(q) + i + u * stride);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        if (i + u * stride < n16) {
+          const uint32_t w[4] = {in[u].x, in[u].y, in[u].z, in[u].w};
+          uint32_t o[4 * OV];
+          if constexpr (sizeof(R) == 2) {
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t b0 = (w[k >> 1] >> (16 * (k & 1))) & 0xffu;
+              const uint32_t b1 = (w[k >> 1] >> (16 * (k & 1) + 8)) & 0xffu;
+              o[k] = my_lut[b0 * 32] | (my_lut[b1 * 32] << 16);
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k) o[k] = my_lut[((w[k >> 2] >> (8 * (k & 3))) & 0xffu) * 32];
+          }
+          uint4* dst = reinterpret_cast<uint4*>(out) + (i + u * stride) * OV;
+#pragma unroll
+          for (int v = 0; v < OV; ++v) __stcs(dst + v, make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]));
         }
-      } else {
-#pragma unroll
-        for (int k = 0; k < 16; ++k) o[k] = my_lut[((w[k >> 2] >> (8 * (k & 3))) & 0xffu) * 32];
       }
-      uint4* dst = reinterpret_cast<uint4*>(out) + i * (16 * sizeof(R) / 16);
-#pragma unroll
-      for (int v = 0; v < static_cast<int>(16 * sizeof(R) / 16); ++v)
-        __stcs(dst + v, make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]));
     }
     done = n16 * 16;
   }
@@ -333,7 +452,9 @@ template <typename T>
 static cudaError_t enc_t(const void* x, int64_t n, const float* scale_in, const uint32_t* partials, int nparts,
                          float* scale_out, void* out, int out_dtype, cudaStream_t st) {
   const bool vec = al16(x) && al16(out);
-  const int grid = grid_for(std::max<int64_t>(n / 16, 1), kEncThreads, 8);
+  const void* kern = (out_dtype == E4M3) ? reinterpret_cast<const void*>(encode_kernel<T, true>)
+                                         : reinterpret_cast<const void*>(encode_kernel<T, false>);
+  const int grid = grid_for(std::max<int64_t>(n / 32, 1), kEncThreads, cached_occupancy(kern, kEncThreads, 0));
   if (out_dtype == E4M3) {
     encode_kernel<T, true><<<grid, kEncThreads, 0, st>>>(static_cast<const T*>(x), n, vec, scale_in, partials, nparts,
                                                          scale_out, static_cast<uint8_t*>(out));
@@ -354,11 +475,68 @@ cudaError_t encode_launch(const void* x, int64_t n, int x_dtype, const float* sc
   }
 }
 
+namespace {
+constexpr size_t kQuantPartialsOffset = 256;
+
+template <typename T, bool E4M3>
+cudaError_t quant_dyn_t(const void* x, int64_t n, float* scale_out, void* out, void* ws, size_t ws_bytes,
+                        cudaStream_t st) {
+  auto kernel = quantize_dynamic_kernel<T, E4M3>;
+  const int occ = cached_occupancy(reinterpret_cast<const void*>(kernel), kQuantThreads, 0);
+  const int64_t want = std::max<int64_t>(1, (n / 16 + kQuantThreads - 1) / kQuantThreads);
+  const int grid = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(occ) * num_sms()));
+  if (ws_bytes < kQuantPartialsOffset + sizeof(uint32_t) * static_cast<size_t>(grid)) return cudaErrorInvalidValue;
+  auto* barrier = static_cast<uint32_t*>(ws);
+  auto* partials = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + kQuantPartialsOffset);
+  cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(uint32_t), st);
+  note_launch();
+  if (e != cudaSuccess) return e;
+  const T* xp = static_cast<const T*>(x);
+  const bool vec = al16(x) && al16(out);
+  auto* op = static_cast<uint8_t*>(out);
+  uint32_t* err = error_word_ptr();
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kQuantThreads);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, xp, n, vec, barrier, partials, scale_out, op, err);
+  note_launch();
+  return e;
+}
+}  // namespace
+
+size_t quantize_dynamic_workspace_bytes() {
+  // at most 4 CTAs of kQuantThreads per SM (2048 threads)
+  return kQuantPartialsOffset + sizeof(uint32_t) * 4 * static_cast<size_t>(num_sms());
+}
+
+cudaError_t quantize_dynamic_launch(const void* x, int64_t n, int x_dtype, float* scale_out, void* out, int out_dtype,
+                                    void* ws, size_t ws_bytes, cudaStream_t st) {
+  const bool e4 = (out_dtype == E4M3);
+  switch (x_dtype) {
+    case F16: return e4 ? quant_dyn_t<__half, true>(x, n, scale_out, out, ws, ws_bytes, st)
+                        : quant_dyn_t<__half, false>(x, n, scale_out, out, ws, ws_bytes, st);
+    case BF16: return e4 ? quant_dyn_t<__nv_bfloat16, true>(x, n, scale_out, out, ws, ws_bytes, st)
+                         : quant_dyn_t<__nv_bfloat16, false>(x, n, scale_out, out, ws, ws_bytes, st);
+    default: return e4 ? quant_dyn_t<float, true>(x, n, scale_out, out, ws, ws_bytes, st)
+                       : quant_dyn_t<float, false>(x, n, scale_out, out, ws, ws_bytes, st);
+  }
+}
+
 template <typename TO>
 static cudaError_t dec_t(const void* q, int64_t n, bool e4m3, const float* scale, void* out, cudaStream_t st) {
   const bool vec = al16(q) && al16(out);
-  // the per-lane tables take 33 KB of shared memory: 4 CTAs per SM
-  const int grid = grid_for(std::max<int64_t>(n / 16, 1), kDecThreads, 4);
+  // the per-lane tables take 33 KB of shared memory per CTA
+  const void* kern = e4m3 ? reinterpret_cast<const void*>(decode_kernel<TO, true>)
+                          : reinterpret_cast<const void*>(decode_kernel<TO, false>);
+  const int per_sm = cached_occupancy(kern, kDecThreads, 0);
+  const int grid = grid_for(std::max<int64_t>(n / 64, 1), kDecThreads, per_sm);
   if (e4m3) {
     decode_kernel<TO, true><<<grid, kDecThreads, 0, st>>>(static_cast<const uint8_t*>(q), n, vec, scale, static_cast<TO*>(out));
   } else {

@@ -150,8 +150,15 @@ struct Fp8Epi {
     const int32_t* corr_col;
     uint32_t* partial;  // split-K: [splits][M][N] raw accumulators
   };
-  __device__ __forceinline__ void operator()(const Params& p, const uint32_t (&r)[1][16], int row, int col0, int M,
-                                             int N, int split) const {
+  // alpha = fp32(codec_k / (sa * sb)), computed once per thread
+  struct State {
+    float alpha;
+  };
+  static __device__ __forceinline__ State init(const Params& p) {
+    return {static_cast<float>(p.codec_k / (static_cast<double>(__ldg(p.sa)) * __ldg(p.sb)))};
+  }
+  __device__ __forceinline__ void operator()(const Params& p, const State& st, const uint32_t (&r)[1][16], int row,
+                                             int col0, int M, int N, int split) const {
     if (row >= M || col0 >= N) return;
     const int valid = min(16, N - col0);
     if (p.partial != nullptr) {
@@ -167,20 +174,29 @@ struct Fp8Epi {
       }
       return;
     }
-    const float alpha = static_cast<float>(p.codec_k / (static_cast<double>(__ldg(p.sa)) * __ldg(p.sb)));
-    const int32_t cr = p.corr_row ? 128 * __ldg(p.corr_row + row) : 0;
+    const float alpha = st.alpha;
     float v[16];
+    if constexpr (INT_ACC) {
+      int32_t cc[16];
+      const int32_t cr = p.corr_row ? 128 * __ldg(p.corr_row + row) : 0;
+      if (p.corr_col && valid == 16) {
+        // the sums array is 256-byte aligned and col0 is a multiple of 16
+        const int4* q = reinterpret_cast<const int4*>(p.corr_col + col0);
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      float a;
-      if constexpr (INT_ACC) {
-        int32_t iv = static_cast<int32_t>(r[0][i]) - cr;
-        if (p.corr_col) iv -= 128 * __ldg(p.corr_col + min(col0 + i, N - 1));
-        a = static_cast<float>(iv);
+        for (int j = 0; j < 4; ++j) {
+          const int4 t = __ldg(q + j);
+          cc[4 * j] = t.x; cc[4 * j + 1] = t.y; cc[4 * j + 2] = t.z; cc[4 * j + 3] = t.w;
+        }
       } else {
-        a = __uint_as_float(r[0][i]);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) cc[i] = p.corr_col ? __ldg(p.corr_col + min(col0 + i, N - 1)) : 0;
       }
-      v[i] = a * alpha;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        v[i] = static_cast<float>(static_cast<int32_t>(r[0][i]) - cr - 128 * cc[i]) * alpha;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[0][i]) * alpha;
     }
     store_row16<TO>(p.out + static_cast<int64_t>(row) * p.ldc + col0, v, valid, p.vec_ok);
   }
@@ -220,7 +236,8 @@ __global__ void __launch_bounds__(256) fp8_splitk_finalize_kernel(const uint32_t
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr int kStages = 4;
+constexpr int kStages = 4;      // 48 KB stages (one CTA per MMA)
+constexpr int kStagesPair = 6;  // 32 KB stages (two CTAs per MMA)
 constexpr int kGroupM = 16;
 
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
@@ -293,33 +310,27 @@ Fp8Plan plan_fp8(const Fp8GemmArgs& g, bool assume_aligned) {
   return p;
 }
 
-template <MmaKind KIND, int BN, typename TO, bool B_MN>
+template <MmaKind KIND, int BN, typename TO, bool B_MN, int CG>
 cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, const Fp8Plan& p,
                             uint32_t idesc, const int32_t* corr_row, const int32_t* corr_col, uint32_t* partial,
                             cudaStream_t st) {
-  using L = GemmLayout<BN, 1, kStages>;
+  constexpr int STAGES = (CG == 2) ? kStagesPair : kStages;
+  using L = GemmLayout<BN, 1, STAGES, CG>;
   constexpr bool INT_ACC = (KIND == MmaKind::I8);
   using Epi = Fp8Epi<TO, INT_ACC>;
-  auto kern = umma_gemm_kernel<KIND, BN, 1, kStages, Epi, B_MN>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L::SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
+  auto kern = umma_gemm_kernel<KIND, BN, 1, STAGES, Epi, B_MN, CG>;
+  const int resident = gemm_resident_units(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, CG);
+  if (resident <= 0) return cudaErrorInvalidConfiguration;
   const double codec_k = INT_ACC ? (448.0 / 127.0) * (448.0 / 127.0) : 1.0;
   typename Epi::Params ep{static_cast<TO*>(g.c), g.sa, g.sb, codec_k, g.N,
                           al16(g.c) && (g.N * sizeof(TO)) % 16 == 0, corr_row, corr_col,
                           p.splits > 1 ? partial : nullptr};
-  const int64_t work = ((g.M + 127) / 128) * ((g.N + BN - 1) / BN) * p.splits;
-  const int grid = static_cast<int>(std::min<int64_t>(work, num_sms()));
-  kern<<<grid, 192, L::SMEM_BYTES, st>>>(ta, tb, tb, static_cast<int>(g.M), static_cast<int>(g.N),
-                                          static_cast<int>(p.Kp), kGroupM, idesc, ep, error_word_ptr(), p.splits);
+  const int64_t work = ((g.M + L::PAIR_M - 1) / L::PAIR_M) * ((g.N + BN - 1) / BN) * p.splits;
+  const int units = static_cast<int>(std::min<int64_t>(work, resident));
+  cudaError_t e = launch_gemm_units(kern, CG, units, L::SMEM_BYTES, st, ta, tb, tb, static_cast<int>(g.M),
+                                    static_cast<int>(g.N), static_cast<int>(p.Kp), kGroupM, idesc, ep,
+                                    error_word_ptr(), p.splits);
   note_launch();
-  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || p.splits == 1) return e;
   const int64_t total = g.M * g.N;
   const int fgrid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, num_sms() * 8)));
@@ -329,21 +340,30 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
   return cudaGetLastError();
 }
 
-template <MmaKind KIND, int BN, bool B_MN>
+template <MmaKind KIND, int BN, bool B_MN, int CG>
 cudaError_t launch_fp8_out(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, const Fp8Plan& p,
                            uint32_t idesc, const int32_t* cr, const int32_t* cc, uint32_t* part, cudaStream_t st) {
   switch (g.out_dtype) {
-    case F16: return launch_fp8_gemm<KIND, BN, __half, B_MN>(ta, tb, g, p, idesc, cr, cc, part, st);
-    case BF16: return launch_fp8_gemm<KIND, BN, __nv_bfloat16, B_MN>(ta, tb, g, p, idesc, cr, cc, part, st);
-    default: return launch_fp8_gemm<KIND, BN, float, B_MN>(ta, tb, g, p, idesc, cr, cc, part, st);
+    case F16: return launch_fp8_gemm<KIND, BN, __half, B_MN, CG>(ta, tb, g, p, idesc, cr, cc, part, st);
+    case BF16: return launch_fp8_gemm<KIND, BN, __nv_bfloat16, B_MN, CG>(ta, tb, g, p, idesc, cr, cc, part, st);
+    default: return launch_fp8_gemm<KIND, BN, float, B_MN, CG>(ta, tb, g, p, idesc, cr, cc, part, st);
   }
+}
+
+// Two-CTA 256 x 256 tiles when the 128 x 256 tiles fill the GPU and M has
+// at least two 128-row blocks.
+inline int pick_cg(const Fp8GemmArgs& g, const Fp8Plan& p) {
+  return (p.bn == 256 && p.splits == 1 && g.M > 128 && pair_mma_enabled()) ? 2 : 1;
 }
 
 template <MmaKind KIND, bool B_MN>
 cudaError_t launch_fp8_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, const Fp8Plan& p,
                           uint32_t idesc, const int32_t* cr, const int32_t* cc, uint32_t* part, cudaStream_t st) {
-  return p.bn == 256 ? launch_fp8_out<KIND, 256, B_MN>(ta, tb, g, p, idesc, cr, cc, part, st)
-                     : launch_fp8_out<KIND, 128, B_MN>(ta, tb, g, p, idesc, cr, cc, part, st);
+  if (p.bn == 256) {
+    return pick_cg(g, p) == 2 ? launch_fp8_out<KIND, 256, B_MN, 2>(ta, tb, g, p, idesc, cr, cc, part, st)
+                              : launch_fp8_out<KIND, 256, B_MN, 1>(ta, tb, g, p, idesc, cr, cc, part, st);
+  }
+  return launch_fp8_out<KIND, 128, B_MN, 1>(ta, tb, g, p, idesc, cr, cc, part, st);
 }
 
 }  // namespace
@@ -438,10 +458,11 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
     if (!make_tmap_kmajor(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.N, g.N, 128)) return cudaErrorInvalidValue;
   } else {
     const int64_t ldb = p.legacy ? p.Kp : g.K;
-    if (!make_tmap_kmajor(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.N, ldb, ldb, p.bn)) return cudaErrorInvalidValue;
+    if (!make_tmap_kmajor(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.N, ldb, ldb, p.bn / pick_cg(g, p)))
+      return cudaErrorInvalidValue;
   }
   const uint32_t c_fmt = codec ? 2u : 1u;  // s32 / f32 accumulators
-  const uint32_t idesc = make_idesc(c_fmt, a_fmt, b_fmt, false, p.b_mn, 128, p.bn);
+  const uint32_t idesc = make_idesc(c_fmt, a_fmt, b_fmt, false, p.b_mn, 128 * pick_cg(g, p), p.bn);
   if (codec) {
     return p.b_mn ? launch_fp8_bn<MmaKind::I8, true>(ta, tb, g, p, idesc, corr_row, corr_col, partial, st)
                   : launch_fp8_bn<MmaKind::I8, false>(ta, tb, g, p, idesc, corr_row, corr_col, partial, st);

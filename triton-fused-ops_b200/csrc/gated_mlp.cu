@@ -24,15 +24,24 @@
 
 namespace tfo {
 
+__device__ __forceinline__ float tanh_approx(float v) {
+  float r;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(r) : "f"(v));
+  return r;
+}
+
+// Activations on the fp32 up-projection. SiLU and tanh-GELU use the
+// hardware's approximate exp2 / reciprocal / tanh (relative errors ~2^-21 to
+// 2^-11, far below the fp16/bf16 output rounding); erf-GELU keeps erff.
 template <int ACT>
 __device__ __forceinline__ float act_fn(float u) {
   if constexpr (ACT == 0) {
-    return u / (1.0f + expf(-u));
+    return __fdividef(u, 1.0f + __expf(-u));
   } else if constexpr (ACT == 1) {
     return 0.5f * u * (1.0f + erff(u * 0.7071067811865476f));
   } else {
-    const float inner = 0.7978845608028654f * (u + 0.044715f * u * u * u);
-    return 0.5f * u * (1.0f + tanhf(inner));
+    const float inner = 0.7978845608028654f * fmaf(0.044715f * u, u * u, u);
+    return 0.5f * u * (1.0f + tanh_approx(inner));
   }
 }
 
@@ -43,8 +52,10 @@ struct GatedEpi {
     int64_t ldc;
     bool vec_ok;
   };
-  __device__ __forceinline__ void operator()(const Params& p, const uint32_t (&r)[2][16], int row, int col0, int M,
-                                             int N, int /*split*/) const {
+  struct State {};
+  static __device__ __forceinline__ State init(const Params&) { return {}; }
+  __device__ __forceinline__ void operator()(const Params& p, const State&, const uint32_t (&r)[2][16], int row,
+                                             int col0, int M, int N, int /*split*/) const {
     if (row >= M || col0 >= N) return;
     float v[16];
 #pragma unroll
@@ -92,7 +103,8 @@ __global__ void to_f32_kernel(const void* __restrict__ src, int64_t n, int dt, f
 
 namespace {
 
-constexpr int kStages = 4;
+constexpr int kStages = 4;      // 48 KB stages (one CTA per MMA)
+constexpr int kStagesPair = 6;  // 32 KB stages (two CTAs per MMA)
 constexpr int kBlockN = 128;
 constexpr int kGroupM = 16;
 
@@ -131,28 +143,33 @@ MlpPlan plan_mlp(const GatedMlpArgs& g) {
   return p;
 }
 
+template <MmaKind KIND, typename TO, int ACT, int CG>
+cudaError_t launch_umma_cg(const CUtensorMap& tx, const CUtensorMap& tg, const CUtensorMap& tu, const GatedMlpArgs& g,
+                           uint32_t idesc, cudaStream_t st) {
+  constexpr int STAGES = (CG == 2) ? kStagesPair : kStages;
+  using L = GemmLayout<kBlockN, 2, STAGES, CG>;
+  using Epi = GatedEpi<TO, ACT>;
+  auto kern = umma_gemm_kernel<KIND, kBlockN, 2, STAGES, Epi, false, CG>;
+  const int resident = gemm_resident_units(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, CG);
+  if (resident <= 0) return cudaErrorInvalidConfiguration;
+  typename Epi::Params ep{static_cast<TO*>(g.out), g.N, al16(g.out) && (g.N * sizeof(TO)) % 16 == 0};
+  const int64_t tiles = ((g.M + L::PAIR_M - 1) / L::PAIR_M) * ((g.N + kBlockN - 1) / kBlockN);
+  const int units = static_cast<int>(std::min<int64_t>(tiles, resident));
+  cudaError_t e = launch_gemm_units(kern, CG, units, L::SMEM_BYTES, st, tx, tg, tu, static_cast<int>(g.M),
+                                    static_cast<int>(g.N), static_cast<int>(g.K), kGroupM, idesc, ep,
+                                    error_word_ptr(), 1);
+  note_launch();
+  return e;
+}
+
+// Two-CTA tiles (M = 256 per MMA, half the shared-memory operand traffic per
+// SM) once there are at least two 128-row blocks.
 template <MmaKind KIND, typename TO, int ACT>
 cudaError_t launch_umma(const CUtensorMap& tx, const CUtensorMap& tg, const CUtensorMap& tu, const GatedMlpArgs& g,
-                        uint32_t idesc, cudaStream_t st) {
-  using L = GemmLayout<kBlockN, 2, kStages>;
-  using Epi = GatedEpi<TO, ACT>;
-  auto kern = umma_gemm_kernel<KIND, kBlockN, 2, kStages, Epi>;
-  static bool attr_set[64] = {false};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L::SMEM_BYTES));
-    if (e != cudaSuccess) return e;
-    attr_set[dev] = true;
-  }
-  typename Epi::Params ep{static_cast<TO*>(g.out), g.N, al16(g.out) && (g.N * sizeof(TO)) % 16 == 0};
-  const int64_t tiles = ((g.M + 127) / 128) * ((g.N + kBlockN - 1) / kBlockN);
-  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms()));
-  kern<<<grid, 192, L::SMEM_BYTES, st>>>(tx, tg, tu, static_cast<int>(g.M), static_cast<int>(g.N),
-                                          static_cast<int>(g.K), kGroupM, idesc, ep, error_word_ptr(), 1);
-  note_launch();
-  return cudaGetLastError();
+                        uint32_t fmt_bits, cudaStream_t st) {
+  if (g.M > 128 && pair_mma_enabled())
+    return launch_umma_cg<KIND, TO, ACT, 2>(tx, tg, tu, g, fmt_bits | make_idesc(0, 0, 0, false, false, 256, 2 * kBlockN), st);
+  return launch_umma_cg<KIND, TO, ACT, 1>(tx, tg, tu, g, fmt_bits | make_idesc(0, 0, 0, false, false, 128, 2 * kBlockN), st);
 }
 
 template <MmaKind KIND, typename TO>
@@ -219,7 +236,7 @@ cudaError_t gated_mlp_launch(const GatedMlpArgs& g, cudaStream_t st) {
         !make_tmap_kmajor(&tu, g.wu, dt, 2, g.N, g.K, g.K, kBlockN))
       return cudaErrorInvalidValue;
     const uint32_t fmt = (g.x_dtype == F16) ? 0u : 1u;
-    return launch_out<MmaKind::F16>(tx, tg, tu, g, make_idesc(1, fmt, fmt, false, false, 128, 2 * kBlockN), st);
+    return launch_out<MmaKind::F16>(tx, tg, tu, g, make_idesc(1, fmt, fmt, false, false, 0, 0), st);
   }
 
   uint8_t* ws = static_cast<uint8_t*>(g.ws);
@@ -242,7 +259,7 @@ cudaError_t gated_mlp_launch(const GatedMlpArgs& g, cudaStream_t st) {
   if (!make_tmap_kmajor(&tx, x, dt, 4, g.M, g.K, g.K, 128) || !make_tmap_kmajor(&tg, wg, dt, 4, g.N, g.K, g.K, kBlockN) ||
       !make_tmap_kmajor(&tu, wu, dt, 4, g.N, g.K, g.K, kBlockN))
     return cudaErrorInvalidValue;
-  return launch_out<MmaKind::TF32>(tx, tg, tu, g, make_idesc(1, 2, 2, false, false, 128, 2 * kBlockN), st);
+  return launch_out<MmaKind::TF32>(tx, tg, tu, g, make_idesc(1, 2, 2, false, false, 0, 0), st);
 }
 
 }  // namespace tfo

@@ -46,16 +46,24 @@ struct TileSched {
   }
 };
 
-template <int BLOCK_N, int NUM_B, int STAGES>
+// Per-CTA shared-memory layout. The UMMA is M = 128 * CG by N = NUM_B *
+// BLOCK_N; each CTA stages 128 rows of A and N / CG rows of B per K block.
+template <int BLOCK_N, int NUM_B, int STAGES, int CG = 1>
 struct GemmLayout {
-  static constexpr int BM = 128;
+  static constexpr int BM = 128;             // A rows (and accumulator lanes) per CTA
+  static constexpr int PAIR_M = BM * CG;     // rows per tile
   static constexpr int A_BYTES = BM * 128;
-  static constexpr int B_BYTES = BLOCK_N * 128;
-  static constexpr int STAGE_BYTES = A_BYTES + NUM_B * B_BYTES;
-  static constexpr int ACC_COLS = NUM_B * BLOCK_N;
+  static constexpr int N_MMA = NUM_B * BLOCK_N;
+  static constexpr int B_ROWS = N_MMA / CG;  // B rows staged by one CTA
+  static constexpr int B_STAGE_BYTES = B_ROWS * 128;
+  static constexpr int STAGE_BYTES = A_BYTES + B_STAGE_BYTES;
+  static constexpr int ACC_COLS = N_MMA;
   static constexpr int TMEM_COLS = 2 * ACC_COLS;
+  static_assert(CG == 1 || CG == 2, "one or two CTAs per MMA");
   static_assert(TMEM_COLS <= 512 && (TMEM_COLS & (TMEM_COLS - 1)) == 0, "TMEM columns must be a power of two <= 512");
-  static_assert(BLOCK_N % 16 == 0 && BLOCK_N >= 16 && NUM_B * BLOCK_N <= 256, "UMMA N for M=128");
+  static_assert(BLOCK_N % 16 == 0 && BLOCK_N >= 16 && N_MMA <= 256, "UMMA N");
+  static_assert(CG == 1 || (B_ROWS % 128 == 0 && (NUM_B == 1 || B_ROWS == BLOCK_N)),
+                "pair MMA: each CTA stages whole 128-row B boxes (one operand each when NUM_B == 2)");
   // dynamic shared memory: ring + barriers + 1 KB for manual alignment
   static constexpr size_t SMEM_BYTES = static_cast<size_t>(STAGES) * STAGE_BYTES + 256 + 1024;
 };
@@ -79,25 +87,35 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 
 // Epi must provide:
 //   struct Params;
-//   __device__ void operator()(const Params&, const uint32_t (&acc)[NUM_B][16], int row, int col0, int M, int N,
-//                              int split)
+//   struct State;  values each epilogue thread derives once from Params
+//   static __device__ State init(const Params&);
+//   __device__ void operator()(const Params&, const State&, const uint32_t (&acc)[NUM_B][16], int row, int col0,
+//                              int M, int N, int split)
 //   called once per 16 accumulator columns per row (row < M not guaranteed).
 //
 // B_MN: the B operand is MN-major (B given as [K, N] with N contiguous, as
-// the reference's fp8_gemm passes it); each stage then holds BLOCK_N / 128
+// the reference's fp8_gemm passes it); each stage then holds B_ROWS / 128
 // boxes of [128 K rows x 128 bytes of N], chained by the descriptor's
 // leading-byte offset. Only for 8-bit operands and NUM_B == 1.
 //
 // k_splits > 1 splits the K loop: work item w covers tile w / k_splits and
 // the K blocks of slice w % k_splits; the epilogue receives the slice index.
-template <MmaKind KIND, int BLOCK_N, int NUM_B, int STAGES, class Epi, bool B_MN = false>
+//
+// CG == 2: launched as clusters of two CTAs (consecutive blockIdx.x). Both
+// CTAs walk the same tile list; CTA r of the pair loads A rows
+// [tile_m + 128 r, +128) and B rows [r * B_ROWS, +B_ROWS) of the tile's N
+// range (for NUM_B == 2: operand r), with the transaction bytes reported to
+// the even CTA's `full` barrier. The even CTA issues the M = 256 MMAs and
+// commits to the `empty` / `tfull` barriers of both CTAs; the epilogue warps
+// of both CTAs release the accumulator on the even CTA's `tempty` barrier.
+template <MmaKind KIND, int BLOCK_N, int NUM_B, int STAGES, class Epi, bool B_MN = false, int CG = 1>
 __global__ void __launch_bounds__(192, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
                      const __grid_constant__ CUtensorMap tmap_b1, int M, int N, int K, int group_m, uint32_t idesc,
                      const typename Epi::Params ep, uint32_t* err, int k_splits) {
   static_assert(!B_MN || (NUM_B == 1 && KindTraits<KIND>::ELEM == 1 && BLOCK_N % 128 == 0),
                 "MN-major B: 8-bit operands, one B operand, BLOCK_N a multiple of 128");
-  using L = GemmLayout<BLOCK_N, NUM_B, STAGES>;
+  using L = GemmLayout<BLOCK_N, NUM_B, STAGES, CG>;
   constexpr int KB_ELEMS = 128 / KindTraits<KIND>::ELEM;
 
   extern __shared__ uint8_t smem_raw[];
@@ -112,7 +130,10 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  TileSched sched{(M + L::BM - 1) / L::BM, (N + BLOCK_N - 1) / BLOCK_N, group_m};
+  const uint32_t rank = (CG == 2) ? (cluster_ctarank() & 1u) : 0u;  // position in the pair
+  const bool leader = (rank == 0);
+  const int unit = blockIdx.x / CG, num_units = gridDim.x / CG;
+  TileSched sched{(M + L::PAIR_M - 1) / L::PAIR_M, (N + BLOCK_N - 1) / BLOCK_N, group_m};
   const int num_tiles = sched.num_tiles();
   const int num_k = (K + KB_ELEMS - 1) / KB_ELEMS;
   const int num_work = num_tiles * k_splits;
@@ -138,7 +159,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], 4 * CG);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -147,11 +168,17 @@ __global__ void __launch_bounds__(192, 1)
     if (NUM_B == 2) tma_prefetch_desc(&tmap_b1);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, L::TMEM_COLS);
-    tmem_relinquish();
+    if constexpr (CG == 2) {
+      tmem_alloc_pair(tmem_slot, L::TMEM_COLS);
+      tmem_relinquish_pair();
+    } else {
+      tmem_alloc(tmem_slot, L::TMEM_COLS);
+      tmem_relinquish();
+    }
   }
   tc_fence_before();
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
@@ -159,33 +186,53 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int it = 0;
-      for (int w = blockIdx.x; w < num_work && !*abort_flag; w += gridDim.x) {
+      for (int w = unit; w < num_work && !*abort_flag; w += num_units) {
         const Work wk = work(w);
-        const int m_blk = wk.m_blk, n_blk = wk.n_blk;
+        const int m_row = wk.m_blk * L::PAIR_M + static_cast<int>(rank) * L::BM;
         for (int kb = wk.kb0; kb < wk.kb1; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!wait_or_abort(&empty[s], ph ^ 1, abort_flag, err, ERR_WAIT_TIMEOUT_PRODUCER)) break;
-          mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
           const int kx = kb * KB_ELEMS;
-          tma_load_2d(sa + s * L::A_BYTES, &tmap_a, &full[s], kx, m_blk * L::BM);
-          if constexpr (B_MN) {
+          uint8_t* a_dst = sa + s * L::A_BYTES;
+          uint8_t* b_dst = sb + s * L::B_STAGE_BYTES;
+          if constexpr (CG == 1) {
+            mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
+            tma_load_2d(a_dst, &tmap_a, &full[s], kx, m_row);
+            if constexpr (B_MN) {
 #pragma unroll
-            for (int c = 0; c < BLOCK_N / 128; ++c)
-              tma_load_2d(sb + s * L::B_BYTES + c * (128 * 128), &tmap_b0, &full[s], n_blk * BLOCK_N + c * 128, kx);
+              for (int c = 0; c < L::B_ROWS / 128; ++c)
+                tma_load_2d(b_dst + c * (128 * 128), &tmap_b0, &full[s], wk.n_blk * BLOCK_N + c * 128, kx);
+            } else {
+              tma_load_2d(b_dst, &tmap_b0, &full[s], kx, wk.n_blk * BLOCK_N);
+              if constexpr (NUM_B == 2) tma_load_2d(b_dst + BLOCK_N * 128, &tmap_b1, &full[s], kx, wk.n_blk * BLOCK_N);
+            }
           } else {
-            tma_load_2d(sb + (s * NUM_B) * L::B_BYTES, &tmap_b0, &full[s], kx, n_blk * BLOCK_N);
-            if constexpr (NUM_B == 2)
-              tma_load_2d(sb + (s * NUM_B + 1) * L::B_BYTES, &tmap_b1, &full[s], kx, n_blk * BLOCK_N);
+            // both CTAs' bytes complete the even CTA's full[s]
+            const uint32_t bar = mapa_shared(smem_u32(&full[s]), 0);
+            if (leader) mbar_arrive_expect_tx(&full[s], 2 * L::STAGE_BYTES);
+            tma_load_2d_pair(a_dst, &tmap_a, bar, kx, m_row);
+            if constexpr (B_MN) {
+#pragma unroll
+              for (int c = 0; c < L::B_ROWS / 128; ++c)
+                tma_load_2d_pair(b_dst + c * (128 * 128), &tmap_b0, bar,
+                                 wk.n_blk * BLOCK_N + static_cast<int>(rank) * L::B_ROWS + c * 128, kx);
+            } else if constexpr (NUM_B == 2) {
+              tma_load_2d_pair(b_dst, rank == 0 ? &tmap_b0 : &tmap_b1, bar, kx, wk.n_blk * BLOCK_N);
+            } else {
+              tma_load_2d_pair(b_dst, &tmap_b0, bar, kx, wk.n_blk * BLOCK_N + static_cast<int>(rank) * L::B_ROWS);
+            }
           }
         }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (lane == 0 && leader) {
+      // pair commits go to this CTA's and the peer's barrier at the same offset
+      const uint32_t peer = rank ^ 1u;
       int it = 0, tcount = 0;
-      for (int w = blockIdx.x; w < num_work && !*abort_flag; w += gridDim.x, ++tcount) {
+      for (int w = unit; w < num_work && !*abort_flag; w += num_units, ++tcount) {
         const Work wk = work(w);
         const int kb0 = wk.kb0, kb1 = wk.kb1;
         const int acc = tcount & 1;
@@ -200,39 +247,53 @@ __global__ void __launch_bounds__(192, 1)
           if (!wait_or_abort(&full[s], ph, abort_flag, err, ERR_WAIT_TIMEOUT_MMA)) { ok = false; break; }
           tc_fence_after();
           const uint32_t a_addr = smem_u32(sa + s * L::A_BYTES);
-          const uint32_t b_addr = smem_u32(sb + (s * NUM_B) * L::B_BYTES);
-          // The NUM_B B tiles of a stage are consecutive 128-byte-swizzled
-          // K-major tiles, i.e. one (NUM_B * BLOCK_N)-row tile, so a single
-          // UMMA of N = NUM_B * BLOCK_N reads the A tile once for all of them;
-          // accumulator column j * BLOCK_N + c belongs to B operand j.
+          const uint32_t b_addr = smem_u32(sb + s * L::B_STAGE_BYTES);
+          // With CG == 1 the NUM_B B tiles of a stage are consecutive
+          // 128-byte-swizzled K-major tiles, i.e. one (NUM_B * BLOCK_N)-row
+          // tile, so a single UMMA of N = NUM_B * BLOCK_N reads the A tile
+          // once for all of them; accumulator column j * BLOCK_N + c belongs
+          // to B operand j. With CG == 2 the two halves of N sit in the two
+          // CTAs at the same offset.
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             const uint64_t adesc = smem_desc_kmajor_sw128(a_addr + kk * 32);
             // MN-major B: 32 K rows of 128 bytes per instruction = 4 swizzle atoms
             const uint64_t bdesc = B_MN ? smem_desc_mnmajor_sw128(b_addr + kk * 4096, 128 * 128)
                                         : smem_desc_kmajor_sw128(b_addr + kk * 32);
-            umma<KIND>(d_tmem, adesc, bdesc, idesc, (kb != kb0 || kk != 0) ? 1u : 0u);
+            const uint32_t accum = (kb != kb0 || kk != 0) ? 1u : 0u;
+            if constexpr (CG == 2) umma_pair<KIND>(d_tmem, adesc, bdesc, idesc, accum);
+            else umma<KIND>(d_tmem, adesc, bdesc, idesc, accum);
           }
-          umma_commit(&empty[s]);
+          if constexpr (CG == 2) {
+            umma_commit_pair(smem_u32(&empty[s]));
+            umma_commit_pair(mapa_shared(smem_u32(&empty[s]), peer));
+          } else {
+            umma_commit(&empty[s]);
+          }
         }
         if (!ok) break;
-        umma_commit(&tfull[acc]);
+        if constexpr (CG == 2) {
+          umma_commit_pair(smem_u32(&tfull[acc]));
+          umma_commit_pair(mapa_shared(smem_u32(&tfull[acc]), peer));
+        } else {
+          umma_commit(&tfull[acc]);
+        }
       }
     }
   } else {
     // ------------------------------------------------------------ epilogue
     const int sub = warp & 3;
-    const int row_in_tile = sub * 32 + lane;
+    const int row_in_tile = static_cast<int>(rank) * L::BM + sub * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
+    const typename Epi::State est = Epi::init(ep);
     int tcount = 0;
-    for (int w = blockIdx.x; w < num_work; w += gridDim.x, ++tcount) {
+    for (int w = unit; w < num_work; w += num_units, ++tcount) {
       const int acc = tcount & 1;
       const uint32_t aph = (tcount >> 1) & 1;
       if (!wait_or_abort(&tfull[acc], aph, abort_flag, err, ERR_WAIT_TIMEOUT_EPILOGUE)) break;
       tc_fence_after();
       const Work wk = work(w);
-      const int m_blk = wk.m_blk, n_blk = wk.n_blk, split = wk.split;
-      const int row = m_blk * L::BM + row_in_tile;
+      const int row = wk.m_blk * L::PAIR_M + row_in_tile;
       const uint32_t base = tmem_base + lane_addr + acc * L::ACC_COLS;
 #pragma unroll 1
       for (int c = 0; c < BLOCK_N; c += 16) {
@@ -240,19 +301,24 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N + c, r[j]);
         tmem_ld_wait();
-        Epi{}(ep, r, row, n_blk * BLOCK_N + c, M, N, split);
+        Epi{}(ep, est, r, row, wk.n_blk * BLOCK_N + c, M, N, wk.split);
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
+      if (lane == 0) {
+        if constexpr (CG == 2) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+        else mbar_arrive(&tempty[acc]);
+      }
     }
   }
 
   __syncthreads();
+  if constexpr (CG == 2) cluster_sync();  // no CTA leaves while its pair may still touch its memory
   if (warp == 1) {
     __syncwarp();
     tc_fence_after();
-    tmem_dealloc(tmem_base, L::TMEM_COLS);
+    if constexpr (CG == 2) tmem_dealloc_pair(tmem_base, L::TMEM_COLS);
+    else tmem_dealloc(tmem_base, L::TMEM_COLS);
   }
 }
 
