@@ -63,6 +63,27 @@ TFO_API const char* tfo_last_error(void);
  * device error word that kernels set when a bounded wait expires. */
 TFO_API int tfo_device_error_flags(uint32_t* flags, int clear);
 
+/* The launch configuration the library picks for a problem shape: the static,
+ * shape-keyed table that replaces the reference's autotuner
+ * (triton_ops/autotuner/autotuner.py; its ops launch fixed block sizes).
+ *   op TFO_OP_FP8_GEMM:     M, N, K, aux = TFO_DTYPE_U8 or _E4M3 ([K, N] B,
+ *                           16-byte-aligned operands);
+ *                           out = {tile rows, tile columns, CTAs per MMA,
+ *                           pipeline stages, K splits, group_m}
+ *   op TFO_OP_GATED_MLP:    M, N, K (16-bit operands); out as above
+ *   op TFO_OP_RMSNORM_ROPE: M = rows, N = hidden, K = head_dim, aux = x dtype
+ *                           (16-byte-aligned x/out, heads = hidden / head_dim);
+ *                           out = {kernel (0 generic, 1 CTA per row, 2 warp per
+ *                           row), threads per CTA or rows per CTA, 16-byte
+ *                           vectors per thread or lane, all columns rotated,
+ *                           dynamic shared bytes, 0}
+ * Writes min(n_out, 6) values. Needs no GPU when the device cannot be
+ * queried (148 SMs are assumed). No counterpart in the reference. */
+#define TFO_OP_FP8_GEMM 0
+#define TFO_OP_GATED_MLP 1
+#define TFO_OP_RMSNORM_ROPE 2
+TFO_API int tfo_select_tile(int op, int64_t M, int64_t N, int64_t K, int aux, int32_t* out, int n_out);
+
 /* Launches a one-thread kernel that waits on a barrier nothing will complete,
  * giving up after budget_cycles SM cycles (<= 2^32) and setting the
  * wait-timeout bit of the device error word, exactly as a GEMM pipeline wait

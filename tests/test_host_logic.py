@@ -94,13 +94,41 @@ def test_tile_table_rules():
     from triton_ops.autotuner import tile_table as tt
 
     assert tt.fp8_gemm_config(8192, 4096, 4096)["BLOCK_N"] == 256
+    assert tt.fp8_gemm_config(8192, 4096, 4096)["CTAS_PER_MMA"] == 2
     assert tt.fp8_gemm_config(16, 4096, 4096)["BLOCK_N"] == 128
+    assert tt.fp8_gemm_config(16, 4096, 4096)["SPLIT_K"] == 4
     assert tt.fp8_gemm_config(4096, 96, 4096)["BLOCK_N"] == 128
     c = tt.rmsnorm_rope_config(4096, 64)
-    assert c == {"path": 1, "threads": 256, "vectors_per_thread": 2}
-    assert tt.rmsnorm_rope_config(4100, 64)["path"] == 0  # rows not a whole number of 16-byte vectors
-    assert tt.rmsnorm_rope_config(4096, 48)["path"] == 0  # 48/8 = 6 vectors per head: generic path
-    assert tt.gated_mlp_config(2048, 11264, 4096)["BLOCK_N"] == 128
+    assert c["kernel"] == 1 and c["threads"] == 256 and c["vectors"] == 2
+    assert tt.rmsnorm_rope_config(4096, 64, rows=65536)["kernel"] == 2
+    assert tt.rmsnorm_rope_config(4100, 64)["kernel"] == 0  # rows not a whole number of 16-byte vectors
+    assert tt.rmsnorm_rope_config(4096, 48)["kernel"] == 0  # 48/8 = 6 vectors per head: generic path
+    assert tt.gated_mlp_config(2048, 11264, 4096)["BLOCK_M"] == 256
+
+
+def test_tile_table_matches_library():
+    """The Python statement of the launch table equals the library's own choice (tfo_select_tile)."""
+    import os
+
+    from triton_ops import _lib
+    from triton_ops.autotuner import tile_table as tt
+
+    pair = os.environ.get("TFO_B200_PAIR_MMA", "1") != "0"
+    keys = ("BLOCK_M", "BLOCK_N", "CTAS_PER_MMA", "STAGES", "SPLIT_K", "GROUP_M")
+    for M in (1, 16, 100, 128, 129, 256, 1000, 1024, 4096, 8192, 65536):
+        for N in (64, 128, 129, 1000, 4096, 11264, 40000):
+            for K in (16, 128, 512, 4096):
+                want = [tt.fp8_gemm_config(M, N, K, pair=pair)[k] for k in keys]
+                assert _lib.select_tile(_lib.OP_FP8_GEMM, M, N, K, _lib.U8) == want, (M, N, K)
+                want = [tt.gated_mlp_config(M, N, K, pair=pair)[k] for k in keys]
+                assert _lib.select_tile(_lib.OP_GATED_MLP, M, N, K, _lib.F16) == want, (M, N, K)
+    rk = ("kernel", "threads", "vectors", "full", "smem")
+    for rows in (1, 256, 4096, 8192, 65536):
+        for hidden, hd in ((4096, 64), (4096, 128), (2048, 64), (1024, 32), (8192, 128), (4096, 48), (4100, 50),
+                           (5120, 128), (16384, 128)):
+            for code, eb in ((_lib.F16, 2), (_lib.BF16, 2), (_lib.F32, 4)):
+                want = [tt.rmsnorm_rope_config(hidden, hd, eb, rows=rows)[k] for k in rk] + [0]
+                assert _lib.select_tile(_lib.OP_RMSNORM_ROPE, rows, hidden, hd, code) == want, (rows, hidden, hd, eb)
 
 
 def test_autotuner_and_cache_roundtrip(tmp_path):

@@ -201,6 +201,31 @@ int tfo_rmsnorm_rope(const void* x, const void* weight, const void* cos, const v
 
 size_t tfo_fp8_scale_workspace_bytes(int64_t numel) { return scale_workspace_bytes(numel); }
 
+int tfo_select_tile(int op, int64_t M, int64_t N, int64_t K, int aux, int32_t* out, int n_out) {
+  if (!out || n_out < 0) return fail(TFO_ERR_INVALID, "tfo_select_tile: NULL output");
+  if (M < 0 || N < 0 || K < 0) return fail(TFO_ERR_INVALID, "tfo_select_tile: negative size");
+  int32_t v[6] = {0, 0, 0, 0, 0, 0};
+  if (op == TFO_OP_FP8_GEMM) {
+    if (aux != U8 && aux != E4M3) return fail(TFO_ERR_DTYPE, "tfo_select_tile: fp8_gemm takes U8 or E4M3");
+    fp8_gemm_tile(M, N, K, aux, 0, v);
+  } else if (op == TFO_OP_GATED_MLP) {
+    gated_mlp_tile(M, N, K, v);
+  } else if (op == TFO_OP_RMSNORM_ROPE) {
+    if (!is_float_dtype(aux)) return fail(TFO_ERR_DTYPE, "tfo_select_tile: rmsnorm_rope x must be f16, bf16 or f32");
+    if (K <= 0) return fail(TFO_ERR_INVALID, "tfo_select_tile: head_dim must be positive");
+    const RmsPlan p = rmsnorm_rope_plan(M, N, K, N / K, aux == F32 ? 4 : 2, true);
+    v[0] = p.kind;
+    v[1] = p.threads;
+    v[2] = p.vec;
+    v[3] = p.full ? 1 : 0;
+    v[4] = static_cast<int32_t>(p.smem);
+  } else {
+    return fail(TFO_ERR_INVALID, "tfo_select_tile: unknown op");
+  }
+  for (int i = 0; i < std::min(n_out, 6); ++i) out[i] = v[i];
+  return TFO_OK;
+}
+
 int tfo_fp8_compute_scale(const void* x, int64_t numel, int x_dtype, float* scale_out, void* workspace,
                           size_t workspace_bytes, void* stream) {
   if (!is_float_dtype(x_dtype)) return fail(TFO_ERR_DTYPE, "tfo_fp8_compute_scale: x must be f16, bf16 or f32");

@@ -67,6 +67,16 @@ struct RmsNormRopeArgs {
   int x_dtype, w_dtype, cos_dtype, sin_dtype;
 };
 cudaError_t rmsnorm_rope_launch(const RmsNormRopeArgs& a, cudaStream_t st);
+// Launch choice of tfo_rmsnorm_rope (see rmsnorm_rope_plan in rmsnorm_rope.cu).
+struct RmsPlan {
+  int kind;     // 0 generic, 1 CTA per row, 2 warp per row
+  int threads;  // kind 1: threads per CTA; kind 2: warps (rows) per CTA
+  int vec;      // kind 1: 16-byte vectors per thread; kind 2: per lane
+  bool full;    // every column belongs to a rotated head
+  int cs_stride;
+  size_t smem;
+};
+RmsPlan rmsnorm_rope_plan(int64_t rows, int64_t hidden, int64_t head_dim, int64_t num_heads, int esz, bool vec_ok);
 
 // FP8 codec (fp8_codec.cu)
 int amax_partials_count(int64_t n);
@@ -99,7 +109,11 @@ struct Fp8GemmArgs {
   size_t ws_bytes;
 };
 size_t fp8_gemm_workspace_bytes(const Fp8GemmArgs& g);
-int fp8_gemm_block_n(int64_t M, int64_t N);
+// Launch choice of tfo_fp8_gemm for 16-byte-aligned operands: out = {rows
+// per tile, columns per tile, CTAs per MMA, stages, K splits, group_m}.
+void fp8_gemm_tile(int64_t M, int64_t N, int64_t K, int ab_dtype, int b_layout, int32_t out[6]);
+// Same for tfo_gated_mlp with 16-bit operands.
+void gated_mlp_tile(int64_t M, int64_t N, int64_t K, int32_t out[6]);
 cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st);
 
 // Gated MLP (gated_mlp.cu): out[M, N] = (x Wg^T) * act(x Wu^T), x [M, K], W [N, K].

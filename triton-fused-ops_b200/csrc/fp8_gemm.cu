@@ -256,14 +256,23 @@ struct Fp8Plan {
   bool prep_a, prep_b;  // legacy: both; direct + codec: exactly one
   bool b_mn;            // B read MN-major from [K, N]
   size_t off_a, off_b, off_sum, off_part, bytes;
-  int bn, splits;
+  int bn, cg, splits;
 };
 
-int pick_block_n(int64_t M, int64_t N, bool b_mn) {
-  const int64_t mb = (M + 127) / 128;
-  if (N <= 128) return 128;
-  return (mb * ((N + 255) / 256) >= num_sms()) ? 256 : 128;
-  (void)b_mn;
+// Tile shape: 256-column tiles, as two-CTA 256 x 256 tiles when M has more
+// than one 128-row block (half the operand bytes per SM of 128 x 256 tiles);
+// for M <= 128, 128-column tiles unless the 256-column ones already cover the
+// GPU. K is split when the tiles alone cannot occupy half the GPU.
+void pick_tiles(int64_t M, int64_t N, int64_t Kp, Fp8Plan& p) {
+  const int sms = num_sms();
+  p.bn = 256;
+  if (N <= 128 || (M <= 128 && ((N + 255) / 256) < sms)) p.bn = 128;
+  p.cg = (p.bn == 256 && M > 128 && pair_mma_enabled()) ? 2 : 1;
+  const int64_t tiles = ((M + 128 * p.cg - 1) / (128 * p.cg)) * ((N + p.bn - 1) / p.bn);
+  const int64_t units = sms / p.cg;
+  const int64_t num_k = (Kp + 127) / 128;
+  p.splits = 1;
+  if (tiles < units / 2) p.splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_k / 4, units / tiles)));
 }
 
 Fp8Plan plan_fp8(const Fp8GemmArgs& g, bool assume_aligned) {
@@ -296,14 +305,7 @@ Fp8Plan plan_fp8(const Fp8GemmArgs& g, bool assume_aligned) {
     p.off_sum = off;
     if (codec) off += round_up(4 * (p.prep_a ? g.M : g.N), 256);
   }
-  p.bn = pick_block_n(g.M, g.N, p.b_mn);
-  // split K when the tiles alone cannot occupy the GPU
-  const int64_t tiles = ((g.M + 127) / 128) * ((g.N + p.bn - 1) / p.bn);
-  const int64_t num_k = (p.Kp + 127) / 128;
-  p.splits = 1;
-  if (tiles < num_sms() / 2) {
-    p.splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_k / 4, num_sms() / tiles)));
-  }
+  pick_tiles(g.M, g.N, p.Kp, p);
   p.off_part = off;
   if (p.splits > 1) off += round_up(static_cast<int64_t>(p.splits) * g.M * g.N * 4, 256);
   p.bytes = off;
@@ -350,18 +352,12 @@ cudaError_t launch_fp8_out(const CUtensorMap& ta, const CUtensorMap& tb, const F
   }
 }
 
-// Two-CTA 256 x 256 tiles when the 128 x 256 tiles fill the GPU and M has
-// at least two 128-row blocks.
-inline int pick_cg(const Fp8GemmArgs& g, const Fp8Plan& p) {
-  return (p.bn == 256 && p.splits == 1 && g.M > 128 && pair_mma_enabled()) ? 2 : 1;
-}
-
 template <MmaKind KIND, bool B_MN>
 cudaError_t launch_fp8_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, const Fp8Plan& p,
                           uint32_t idesc, const int32_t* cr, const int32_t* cc, uint32_t* part, cudaStream_t st) {
   if (p.bn == 256) {
-    return pick_cg(g, p) == 2 ? launch_fp8_out<KIND, 256, B_MN, 2>(ta, tb, g, p, idesc, cr, cc, part, st)
-                              : launch_fp8_out<KIND, 256, B_MN, 1>(ta, tb, g, p, idesc, cr, cc, part, st);
+    return p.cg == 2 ? launch_fp8_out<KIND, 256, B_MN, 2>(ta, tb, g, p, idesc, cr, cc, part, st)
+                     : launch_fp8_out<KIND, 256, B_MN, 1>(ta, tb, g, p, idesc, cr, cc, part, st);
   }
   return launch_fp8_out<KIND, 128, B_MN, 1>(ta, tb, g, p, idesc, cr, cc, part, st);
 }
@@ -379,7 +375,21 @@ size_t fp8_gemm_workspace_bytes(const Fp8GemmArgs& g) {
   return std::max(a.bytes, b.bytes);
 }
 
-int fp8_gemm_block_n(int64_t M, int64_t N) { return pick_block_n(M, N, false); }
+void fp8_gemm_tile(int64_t M, int64_t N, int64_t K, int ab_dtype, int b_layout, int32_t out[6]) {
+  Fp8GemmArgs g{};
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.ab_dtype = ab_dtype;
+  g.b_layout = b_layout;
+  const Fp8Plan p = plan_fp8(g, true);
+  out[0] = 128 * p.cg;
+  out[1] = p.bn;
+  out[2] = p.cg;
+  out[3] = p.cg == 2 ? kStagesPair : kStages;
+  out[4] = p.splits;
+  out[5] = kGroupM;
+}
 
 cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
   const Fp8Plan p = plan_fp8(g, false);
@@ -458,11 +468,11 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
     if (!make_tmap_kmajor(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.N, g.N, 128)) return cudaErrorInvalidValue;
   } else {
     const int64_t ldb = p.legacy ? p.Kp : g.K;
-    if (!make_tmap_kmajor(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.N, ldb, ldb, p.bn / pick_cg(g, p)))
+    if (!make_tmap_kmajor(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.N, ldb, ldb, p.bn / p.cg))
       return cudaErrorInvalidValue;
   }
   const uint32_t c_fmt = codec ? 2u : 1u;  // s32 / f32 accumulators
-  const uint32_t idesc = make_idesc(c_fmt, a_fmt, b_fmt, false, p.b_mn, 128 * pick_cg(g, p), p.bn);
+  const uint32_t idesc = make_idesc(c_fmt, a_fmt, b_fmt, false, p.b_mn, 128 * p.cg, p.bn);
   if (codec) {
     return p.b_mn ? launch_fp8_bn<MmaKind::I8, true>(ta, tb, g, p, idesc, corr_row, corr_col, partial, st)
                   : launch_fp8_bn<MmaKind::I8, false>(ta, tb, g, p, idesc, corr_row, corr_col, partial, st);

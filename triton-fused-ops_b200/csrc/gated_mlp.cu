@@ -223,6 +223,18 @@ cudaError_t convert(const void* src, int64_t n, int dt, float* dst, cudaStream_t
 
 size_t gated_mlp_workspace_bytes(const GatedMlpArgs& g) { return plan_mlp(g).bytes; }
 
+void gated_mlp_tile(int64_t M, int64_t N, int64_t K, int32_t out[6]) {
+  (void)N;
+  (void)K;
+  const int cg = (M > 128 && pair_mma_enabled()) ? 2 : 1;
+  out[0] = 128 * cg;
+  out[1] = kBlockN;
+  out[2] = cg;
+  out[3] = cg == 2 ? kStagesPair : kStages;
+  out[4] = 1;
+  out[5] = kGroupM;
+}
+
 cudaError_t gated_mlp_launch(const GatedMlpArgs& g, cudaStream_t st) {
   const MlpPlan p = plan_mlp(g);
   if (p.path == Path::SIMT) return launch_simt(g, st);

@@ -295,13 +295,25 @@ __global__ void __launch_bounds__(192, 1)
       const Work wk = work(w);
       const int row = wk.m_blk * L::PAIR_M + row_in_tile;
       const uint32_t base = tmem_base + lane_addr + acc * L::ACC_COLS;
-#pragma unroll 1
-      for (int c = 0; c < BLOCK_N; c += 16) {
-        uint32_t r[NUM_B][16];
+      // Two register sets: the TMEM load of the next 16 columns is in flight
+      // while the current ones are converted and stored.
+      static_assert(BLOCK_N % 32 == 0, "epilogue walks 32 columns per iteration");
+      uint32_t ra[NUM_B][16], rb[NUM_B][16];
 #pragma unroll
-        for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N + c, r[j]);
+      for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N, ra[j]);
+      tmem_ld_wait();
+#pragma unroll 1
+      for (int c = 0; c < BLOCK_N; c += 32) {
+#pragma unroll
+        for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N + c + 16, rb[j]);
+        Epi{}(ep, est, ra, row, wk.n_blk * BLOCK_N + c, M, N, wk.split);
         tmem_ld_wait();
-        Epi{}(ep, est, r, row, wk.n_blk * BLOCK_N + c, M, N, wk.split);
+        if (c + 32 < BLOCK_N) {
+#pragma unroll
+          for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N + c + 32, ra[j]);
+        }
+        Epi{}(ep, est, rb, row, wk.n_blk * BLOCK_N + c + 16, M, N, wk.split);
+        tmem_ld_wait();
       }
       tc_fence_before();
       __syncwarp();

@@ -596,43 +596,28 @@ cudaError_t launch_warp_rows(const RmsNormRopeArgs& a, int vpl, int warps, int c
 }
 
 template <typename TX, typename TCS>
-cudaError_t pick_nv(const RmsNormRopeArgs& a, int nvec, cudaStream_t st) {
-  for (int nv : {1, 2, 4, 8}) {
-    const int threads = ((nvec + nv - 1) / nv + 31) / 32 * 32;
-    if (threads <= 256) {
-      const bool full = (nv * threads == nvec) && (a.num_heads * a.head_dim == a.hidden);
-      switch (nv) {
-        case 1: return full ? launch_vec<TX, TCS, 1, true>(a, threads, st) : launch_vec<TX, TCS, 1, false>(a, threads, st);
-        case 2: return full ? launch_vec<TX, TCS, 2, true>(a, threads, st) : launch_vec<TX, TCS, 2, false>(a, threads, st);
-        case 4: return full ? launch_vec<TX, TCS, 4, true>(a, threads, st) : launch_vec<TX, TCS, 4, false>(a, threads, st);
-        default: return full ? launch_vec<TX, TCS, 8, true>(a, threads, st) : launch_vec<TX, TCS, 8, false>(a, threads, st);
-      }
-    }
+cudaError_t launch_cta_vec(const RmsNormRopeArgs& a, const RmsPlan& p, cudaStream_t st) {
+  switch (p.vec) {
+    case 1: return p.full ? launch_vec<TX, TCS, 1, true>(a, p.threads, st) : launch_vec<TX, TCS, 1, false>(a, p.threads, st);
+    case 2: return p.full ? launch_vec<TX, TCS, 2, true>(a, p.threads, st) : launch_vec<TX, TCS, 2, false>(a, p.threads, st);
+    case 4: return p.full ? launch_vec<TX, TCS, 4, true>(a, p.threads, st) : launch_vec<TX, TCS, 4, false>(a, p.threads, st);
+    default: return p.full ? launch_vec<TX, TCS, 8, true>(a, p.threads, st) : launch_vec<TX, TCS, 8, false>(a, p.threads, st);
   }
-  return cudaErrorInvalidConfiguration;
 }
 
 template <typename TX>
-cudaError_t dispatch_cs(const RmsNormRopeArgs& a, int nvec, cudaStream_t st) {
-  // warp-per-row kernel: 4, 8 or 16 vectors per lane, enough rows to fill the GPU
-  int cs_stride = 0;
-  size_t smem = 0;
-  const int vpl = nvec / 32;
-  const bool vpl_ok = (nvec % 32 == 0) && (vpl == 4 || vpl == 8 || vpl == 16);
-  const int warps =
-      vpl_ok ? warp_rows_config(a.hidden, a.head_dim, sizeof(TX), warp_rows_max_warps(vpl), &cs_stride, &smem) : 0;
-  if (warps > 0 && a.batch * a.seq_len >= 2ll * num_sms() * warps) {
+cudaError_t dispatch_plan(const RmsNormRopeArgs& a, const RmsPlan& p, cudaStream_t st) {
+  if (p.kind == 2) {
     switch (a.cos_dtype) {
-      case F16: return launch_warp_rows<TX, __half>(a, vpl, warps, cs_stride, smem, st);
-      case BF16: return launch_warp_rows<TX, __nv_bfloat16>(a, vpl, warps, cs_stride, smem, st);
-      default: return launch_warp_rows<TX, float>(a, vpl, warps, cs_stride, smem, st);
+      case F16: return launch_warp_rows<TX, __half>(a, p.vec, p.threads, p.cs_stride, p.smem, st);
+      case BF16: return launch_warp_rows<TX, __nv_bfloat16>(a, p.vec, p.threads, p.cs_stride, p.smem, st);
+      default: return launch_warp_rows<TX, float>(a, p.vec, p.threads, p.cs_stride, p.smem, st);
     }
   }
   switch (a.cos_dtype) {
-    case F16: return pick_nv<TX, __half>(a, nvec, st);
-    case BF16:
-      return pick_nv<TX, __nv_bfloat16>(a, nvec, st);
-    default: return pick_nv<TX, float>(a, nvec, st);
+    case F16: return launch_cta_vec<TX, __half>(a, p, st);
+    case BF16: return launch_cta_vec<TX, __nv_bfloat16>(a, p, st);
+    default: return launch_cta_vec<TX, float>(a, p, st);
   }
 }
 
@@ -662,19 +647,58 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 }  // namespace
 
 // Chooses the vectorised path when the row, head and table layout allow it.
+// Kernel choice for a shape (the static launch table):
+//  * kind 2, warp per row: the row is 4, 8 or 16 16-byte vectors per lane and
+//    there are at least two rows per warp slot of a full wave;
+//  * kind 1, CTA per row: `threads` threads with `vec` 16-byte vectors each;
+//  * kind 0, generic: any shape, dtype mix or alignment.
+RmsPlan rmsnorm_rope_plan(int64_t rows, int64_t hidden, int64_t head_dim, int64_t num_heads, int esz, bool vec_ok) {
+  RmsPlan p{};
+  p.kind = 0;
+  p.threads = 256;
+  const int E = 16 / esz;
+  const int64_t D = head_dim;
+  const int64_t dv = D / E;
+  const bool vec = vec_ok && (hidden % E == 0) && (D % (2 * E) == 0) && dv >= 2 && dv <= 32 && (dv & (dv - 1)) == 0 &&
+                   (hidden / E) <= 8 * 256;
+  if (!vec) return p;
+  const int nvec = static_cast<int>(hidden / E);
+  const int vpl = nvec / 32;
+  const bool vpl_ok = (nvec % 32 == 0) && (vpl == 4 || vpl == 8 || vpl == 16);
+  int cs_stride = 0;
+  size_t smem = 0;
+  const int warps = vpl_ok ? warp_rows_config(hidden, D, esz, warp_rows_max_warps(vpl), &cs_stride, &smem) : 0;
+  if (warps > 0 && rows >= 2ll * num_sms() * warps) {
+    p.kind = 2;
+    p.threads = warps;
+    p.vec = vpl;
+    p.full = (num_heads * D == hidden);
+    p.cs_stride = cs_stride;
+    p.smem = smem;
+    return p;
+  }
+  for (int nv : {1, 2, 4, 8}) {
+    const int threads = ((nvec + nv - 1) / nv + 31) / 32 * 32;
+    if (threads <= 256) {
+      p.kind = 1;
+      p.threads = threads;
+      p.vec = nv;
+      p.full = (nv * threads == nvec) && (num_heads * D == hidden);
+      return p;
+    }
+  }
+  return p;
+}
+
 cudaError_t rmsnorm_rope_launch(const RmsNormRopeArgs& a, cudaStream_t st) {
   const int esz = (a.x_dtype == F32) ? 4 : 2;
-  const int E = 16 / esz;
-  const int64_t D = a.head_dim;
-  const int64_t dv = D / E;
-  bool vec = aligned16(a.x) && aligned16(a.out) && (a.hidden % E == 0) && (D % (2 * E) == 0) && dv >= 2 &&
-             dv <= 32 && (dv & (dv - 1)) == 0 && (a.hidden / E) <= 8 * 256 && a.cos_dtype == a.sin_dtype;
-  if (vec) {
-    const int nvec = static_cast<int>(a.hidden / E);
+  const bool vec_ok = aligned16(a.x) && aligned16(a.out) && a.cos_dtype == a.sin_dtype;
+  const RmsPlan p = rmsnorm_rope_plan(a.batch * a.seq_len, a.hidden, a.head_dim, a.num_heads, esz, vec_ok);
+  if (p.kind != 0) {
     switch (a.x_dtype) {
-      case F16: return dispatch_cs<__half>(a, nvec, st);
-      case BF16: return dispatch_cs<__nv_bfloat16>(a, nvec, st);
-      default: return dispatch_cs<float>(a, nvec, st);
+      case F16: return dispatch_plan<__half>(a, p, st);
+      case BF16: return dispatch_plan<__nv_bfloat16>(a, p, st);
+      default: return dispatch_plan<float>(a, p, st);
     }
   }
   switch (a.x_dtype) {

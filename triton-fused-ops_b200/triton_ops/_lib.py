@@ -52,6 +52,7 @@ _SIGNATURES = {
     "tfo_kernel_launches": (ctypes.c_ulonglong, []),
     "tfo_device_error_flags": (_c_int, [ctypes.POINTER(ctypes.c_uint32), _c_int]),
     "tfo_selftest_bounded_wait": (_c_int, [_c_i64, _c_vp]),
+    "tfo_select_tile": (_c_int, [_c_int, _c_i64, _c_i64, _c_i64, _c_int, ctypes.POINTER(ctypes.c_int32), _c_int]),
     "tfo_rmsnorm_rope": (
         _c_int,
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
@@ -149,6 +150,16 @@ def device_error_flags(clear: bool = True) -> int:
     flags = ctypes.c_uint32(0)
     check(load().tfo_device_error_flags(ctypes.byref(flags), int(clear)), "tfo_device_error_flags")
     return int(flags.value)
+
+
+OP_FP8_GEMM, OP_GATED_MLP, OP_RMSNORM_ROPE = 0, 1, 2
+
+
+def select_tile(op: int, M: int, N: int, K: int, aux: int) -> list:
+    """The library's launch configuration for a shape (six integers, see tfo_select_tile)."""
+    out = (ctypes.c_int32 * 6)()
+    check(load().tfo_select_tile(op, M, N, K, aux, out, 6), "tfo_select_tile")
+    return list(out)
 
 
 def kernel_launches() -> int:
