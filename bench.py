@@ -694,14 +694,19 @@ def run_profile_op(args):
         cos, sin = rope_tables(seq, D, dev)
         fn = lambda: triton_ops.fused_rmsnorm_rope(x, w, cos, sin)
     elif op == "fp8_gemm":
-        m = {"small": 128, "config4": 1024, "prefill": 8192}[shape]
-        qa, sa = triton_ops.quantize_fp8(torch.randn(m, H, device=dev, generator=g).half())
-        qb, sb = triton_ops.quantize_fp8(torch.randn(H, H, device=dev, generator=g).half())
+        m = {"small": 128, "config4": 1024, "config3": 8192, "prefill": 8192}[shape]
+        qd = torch.float8_e4m3fn if args.profile_dtype == "e4m3" else torch.uint8
+        qa, sa = triton_ops.quantize_fp8(torch.randn(m, H, device=dev, generator=g).half(), dtype=qd)
+        qb, sb = triton_ops.quantize_fp8(torch.randn(H, H, device=dev, generator=g).half(), dtype=qd)
         fn = lambda: triton_ops.fp8_gemm(qa, qb, sa, sb)
     elif op in ("quantize", "dequantize"):
+        # [4096, 4096] fp16 N(0, 1) with 0.1% of entries set to +-200
         t = torch.randn(4096, 4096, device=dev, generator=g).half()
-        q, s = triton_ops.quantize_fp8(t)
-        fn = (lambda: triton_ops.quantize_fp8(t)) if op == "quantize" else (lambda: triton_ops.dequantize_fp8(q, s))
+        idx = torch.randperm(t.numel(), device=dev, generator=g)[: t.numel() // 1000]
+        t.view(-1)[idx] = 200.0 * torch.sign(torch.randn(idx.numel(), device=dev, generator=g)).half()
+        qd = torch.float8_e4m3fn if args.profile_dtype == "e4m3" else torch.uint8
+        q, s = triton_ops.quantize_fp8(t, dtype=qd)
+        fn = (lambda: triton_ops.quantize_fp8(t, dtype=qd)) if op == "quantize" else (lambda: triton_ops.dequantize_fp8(q, s))
     else:
         raise SystemExit(f"unknown op {op}")
     for _ in range(args.steps):
@@ -722,7 +727,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-op", default=None,
                     help="run one op --steps times for an ncu capture: gated_mlp, rmsnorm_rope, fp8_gemm, quantize, dequantize")
-    ap.add_argument("--profile-shape", default="small", help="small | config1 | config4 | prefill")
+    ap.add_argument("--profile-shape", default="small", help="small | config1 | config3 | config4 | prefill")
+    ap.add_argument("--profile-dtype", default="u8", choices=["u8", "e4m3"],
+                    help="8-bit code of the fp8_gemm / quantize / dequantize profile runs")
     args = ap.parse_args()
     if args.profile_op:
         return run_profile_op(args)

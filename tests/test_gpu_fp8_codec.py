@@ -85,7 +85,8 @@ def test_all_bf16_bit_patterns(cuda):
     np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(allb, np.float32(0.75)))
 
 
-@pytest.mark.parametrize("n", [1, 15, 16, 17, 1000, 4097, 1 << 20])
+# sizes on both quantize paths: shared-memory resident (up to ~34 MB) and L2 re-read
+@pytest.mark.parametrize("n", [1, 15, 16, 17, 1000, 4097, 1 << 20, (1 << 20) + 7, 3_000_001, 9_000_000])
 @pytest.mark.parametrize("dtype", ["f16", "bf16", "f32"])
 def test_dynamic_scale_sizes(cuda, n, dtype):
     from triton_ops import FP8Format, quantize_fp8

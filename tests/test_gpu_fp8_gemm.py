@@ -179,7 +179,8 @@ def test_validation(cuda):
 # Shapes whose 128 x 256 tiles fill the GPU use two-CTA 256 x 256 tiles; ragged
 # M leaves the second CTA's rows partly or wholly outside the matrix.
 @pytest.mark.parametrize("M,N,K", [(300, 12800, 256), (1000, 4864, 384), (129, 37888, 128), (4095, 4096, 200),
-                                   (256, 4096, 1024), (200, 1024, 2048), (1024, 4096, 4096)])
+                                   (256, 4096, 1024), (200, 1024, 2048), (1024, 4096, 4096),
+                                   (300, 144, 208), (2000, 1040, 4112)])
 def test_pair_tiles_ragged(cuda, M, N, K):
     from triton_ops import fp8_gemm
 

@@ -288,17 +288,13 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   return v;
 }
 
-template <typename T, bool E4M3>
-__global__ void __launch_bounds__(kQuantThreads, 2)
-    quantize_dynamic_kernel(const T* __restrict__ x, int64_t n, bool vec, uint32_t* __restrict__ barrier,
-                            uint32_t* __restrict__ partials, float* __restrict__ scale_out,
-                            uint8_t* __restrict__ out, uint32_t* __restrict__ err) {
-  __shared__ uint32_t red[32];
-  __shared__ float s_sh;
-  __shared__ int ok_sh;
-  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
-  const uint32_t b = block_max_u32(amax_share<T, 4>(x, n, vec, tid, stride), red);
+// Publishes this CTA's partial max and waits (bounded) until every CTA of the
+// grid has published; then returns the scale reduced from all partials (every
+// CTA computes the same value). Returns false if the wait ran out of budget
+// (ERR_GRID_BARRIER is set and the caller must not write its output).
+__device__ __forceinline__ bool grid_publish_and_scale(uint32_t b, uint32_t* __restrict__ barrier,
+                                                       uint32_t* __restrict__ partials, uint32_t* __restrict__ err,
+                                                       uint32_t* red, float* s_sh, int* ok_sh) {
   if (threadIdx.x == 0) {
     partials[blockIdx.x] = b;
     __threadfence();
@@ -316,19 +312,173 @@ __global__ void __launch_bounds__(kQuantThreads, 2)
       }
     }
     __threadfence();
-    ok_sh = ok;
+    *ok_sh = ok;
   }
   __syncthreads();
-  if (!ok_sh) return;
+  if (!*ok_sh) return false;
   const float s = reduce_partials_to_scale(partials, gridDim.x, red);
-  if (threadIdx.x == 0) {
-    s_sh = s;
-    if (blockIdx.x == 0) *scale_out = s;
-  }
+  if (threadIdx.x == 0) *s_sh = s;
   __syncthreads();
+  return true;
+}
+
+template <typename T, bool E4M3>
+__global__ void __launch_bounds__(kQuantThreads, 2)
+    quantize_dynamic_kernel(const T* __restrict__ x, int64_t n, bool vec, uint32_t* __restrict__ barrier,
+                            uint32_t* __restrict__ partials, float* __restrict__ scale_out,
+                            uint8_t* __restrict__ out, uint32_t* __restrict__ err) {
+  __shared__ uint32_t red[32];
+  __shared__ float s_sh;
+  __shared__ int ok_sh;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const uint32_t b = block_max_u32(amax_share<T, 4>(x, n, vec, tid, stride), red);
+  if (!grid_publish_and_scale(b, barrier, partials, err, red, &s_sh, &ok_sh)) return;
   const float sc = s_sh;
+  if (threadIdx.x == 0 && blockIdx.x == 0) *scale_out = sc;
   if (sc > 0.f && sc < INFINITY) encode_share<T, E4M3, 2, true>(x, n, vec, sc, out, tid, stride);
   else encode_share<T, E4M3, 2, false>(x, n, vec, sc, out, tid, stride);
+}
+
+// ---- dynamic-scale quantize with the tensor resident in shared memory -----
+// For tensors that fit in the SMs' shared memory (one CTA per SM, up to
+// kResSlabMax bytes each): every CTA bulk-copies its contiguous slab into
+// shared memory in kResPieces pieces (one mbarrier each) and folds each piece
+// into its max |x| as it lands; CTAs meet at the grid barrier; then each CTA
+// encodes its slab from shared memory. HBM sees one read of x and one write
+// of the codes. 16-byte vectors; the last CTA also covers the n % 16 tail
+// elements from global memory.
+constexpr int kResThreads = 512;
+constexpr int kResPieces = 8;
+constexpr size_t kResSlabMax = 227 * 1024 - 1024;
+
+// max over the |x| bit patterns of one 16-byte vector, kept per 16-bit lane
+// for 16-bit types (|x| orders like its bits; NaN above inf) and per word for fp32
+template <typename T>
+__device__ __forceinline__ uint32_t absmax_vec(uint32_t m, uint4 v) {
+  if constexpr (sizeof(T) == 2) {
+    m = __vmaxu2(m, v.x & 0x7FFF7FFFu);
+    m = __vmaxu2(m, v.y & 0x7FFF7FFFu);
+    m = __vmaxu2(m, v.z & 0x7FFF7FFFu);
+    return __vmaxu2(m, v.w & 0x7FFF7FFFu);
+  } else {
+    m = max(m, v.x & 0x7FFFFFFFu);
+    m = max(m, v.y & 0x7FFFFFFFu);
+    m = max(m, v.z & 0x7FFFFFFFu);
+    return max(m, v.w & 0x7FFFFFFFu);
+  }
+}
+// the fp32 bit pattern of the larger lane
+template <typename T>
+__device__ __forceinline__ uint32_t absmax_to_f32_bits(uint32_t m) {
+  if constexpr (std::is_same<T, float>::value) {
+    return m;
+  } else {
+    const uint32_t h = max(m & 0xFFFFu, m >> 16);
+    if constexpr (std::is_same<T, __half>::value) {
+      return __float_as_uint(__half2float(__ushort_as_half(static_cast<unsigned short>(h))));
+    } else {
+      return h << 16;
+    }
+  }
+}
+
+template <typename T, bool E4M3>
+__global__ void __launch_bounds__(kResThreads, 1)
+    quantize_resident_kernel(const T* __restrict__ x, int64_t n, int64_t vecs_per_cta, uint32_t* __restrict__ barrier,
+                             uint32_t* __restrict__ partials, float* __restrict__ scale_out,
+                             uint8_t* __restrict__ out, uint32_t* __restrict__ err) {
+  constexpr int EV = 16 / sizeof(T);  // elements per 16-byte vector
+  extern __shared__ __align__(128) uint4 slab[];
+  __shared__ uint64_t bars[kResPieces];
+  __shared__ uint32_t red[32];
+  __shared__ float s_sh;
+  __shared__ int ok_sh;
+  const int64_t nvec = n / EV;
+  const int64_t v0 = static_cast<int64_t>(blockIdx.x) * vecs_per_cta;
+  const int64_t v1 = min(nvec, v0 + vecs_per_cta);
+  const int my = v1 > v0 ? static_cast<int>(v1 - v0) : 0;
+  const int per_piece = (my + kResPieces - 1) / kResPieces;
+  if (threadIdx.x == 0) {
+    for (int p = 0; p < kResPieces; ++p) mbar_init(&bars[p], 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int p = 0; p < kResPieces; ++p) {
+      const int a = p * per_piece, b = min(my, a + per_piece);
+      const uint32_t bytes = static_cast<uint32_t>(max(0, b - a)) * 16u;
+      if (bytes > 0) {
+        mbar_arrive_expect_tx(&bars[p], bytes);
+        bulk_load(slab + a, reinterpret_cast<const uint4*>(x) + v0 + a, bytes, &bars[p]);
+      } else {
+        mbar_arrive(&bars[p]);
+      }
+    }
+  }
+  uint32_t m = 0;
+  for (int p = 0; p < kResPieces; ++p) {
+    mbar_wait(&bars[p], 0, err, ERR_WAIT_TIMEOUT_OTHER);  // on expiry: error bit set, values unreliable
+    const int a = p * per_piece, b = min(my, a + per_piece);
+    for (int v = a + threadIdx.x; v < b; v += kResThreads) m = absmax_vec<T>(m, slab[v]);
+  }
+  uint32_t mf = absmax_to_f32_bits<T>(m);
+  if (blockIdx.x == gridDim.x - 1)
+    for (int64_t i = nvec * EV + threadIdx.x; i < n; i += kResThreads)
+      mf = max(mf, __float_as_uint(fabsf(Ty<T>::to_f(x[i]))));
+  const uint32_t bmax = block_max_u32(mf, red);
+  if (!grid_publish_and_scale(bmax, barrier, partials, err, red, &s_sh, &ok_sh)) return;
+  const float s = s_sh;
+  if (threadIdx.x == 0 && blockIdx.x == 0) *scale_out = s;
+  const bool in_range = (s > 0.f && s < INFINITY);
+  for (int v = threadIdx.x; v < my; v += kResThreads) {
+    Chunk<T> c;  // reuse the 16-element converter on half a chunk for 16-bit types
+    const uint4 q = slab[v];
+    float f[16];
+    if constexpr (EV == 8) {
+      c.v[0] = q;
+      c.v[1] = q;
+    } else {
+      c.v[0] = q;
+      c.v[1] = q;
+      c.v[2] = q;
+      c.v[3] = q;
+    }
+    c.to_f(f);
+    uint32_t w[2];
+    if constexpr (E4M3) {
+#pragma unroll
+      for (int h = 0; h < EV / 4; ++h) {
+        const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(__fmul_rn(f[4 * h], s), __fmul_rn(f[4 * h + 1], s)),
+                                                     __NV_SATFINITE, __NV_E4M3);
+        const uint32_t hi = __nv_cvt_float2_to_fp8x2(
+            make_float2(__fmul_rn(f[4 * h + 2], s), __fmul_rn(f[4 * h + 3], s)), __NV_SATFINITE, __NV_E4M3);
+        w[h] = lo | (hi << 16);
+      }
+    } else if (in_range) {
+#pragma unroll
+      for (int h = 0; h < EV / 4; ++h)
+        w[h] = ref_encode4_in_range(__fmul_rn(f[4 * h], s), __fmul_rn(f[4 * h + 1], s), __fmul_rn(f[4 * h + 2], s),
+                                    __fmul_rn(f[4 * h + 3], s));
+    } else {
+#pragma unroll
+      for (int h = 0; h < EV / 4; ++h)
+        w[h] = ref_encode(__fmul_rn(f[4 * h], s)) | (ref_encode(__fmul_rn(f[4 * h + 1], s)) << 8) |
+               (ref_encode(__fmul_rn(f[4 * h + 2], s)) << 16) | (ref_encode(__fmul_rn(f[4 * h + 3], s)) << 24);
+    }
+    if constexpr (EV == 8) {
+      reinterpret_cast<uint2*>(out)[v0 + v] = make_uint2(w[0], w[1]);
+    } else {
+      reinterpret_cast<uint32_t*>(out)[v0 + v] = w[0];
+    }
+  }
+  if (blockIdx.x == gridDim.x - 1) {
+    for (int64_t i = nvec * EV + threadIdx.x; i < n; i += kResThreads) {
+      const float c = __fmul_rn(Ty<T>::to_f(x[i]), s);
+      out[i] = static_cast<uint8_t>(E4M3 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(c, __NV_SATFINITE, __NV_E4M3))
+                                         : ref_encode(c));
+    }
+  }
 }
 
 // ---- decode ----------------------------------------------------------------
@@ -509,6 +659,63 @@ cudaError_t quant_dyn_t(const void* x, int64_t n, float* scale_out, void* out, v
   note_launch();
   return e;
 }
+// The shared-memory-resident variant, when x (16-byte aligned) fits in the
+// SMs' shared memory and is at least 64 vectors per SM; *used tells whether
+// it was launched.
+template <typename T, bool E4M3>
+cudaError_t quant_res_t(const void* x, int64_t n, float* scale_out, void* out, void* ws, size_t ws_bytes,
+                        cudaStream_t st, bool* used) {
+  *used = false;
+  constexpr int EV = 16 / sizeof(T);
+  const int sms = num_sms();
+  const int64_t nvec = n / EV;
+  if (!al16(x) || !al16(out) || nvec < 64ll * sms) return cudaSuccess;
+  const int64_t vpc = (nvec + sms - 1) / sms;
+  const size_t smem = static_cast<size_t>(vpc) * 16;
+  if (smem > kResSlabMax) return cudaSuccess;
+  const int grid = static_cast<int>((nvec + vpc - 1) / vpc);
+  if (ws_bytes < kQuantPartialsOffset + sizeof(uint32_t) * static_cast<size_t>(grid)) return cudaErrorInvalidValue;
+  auto kernel = quantize_resident_kernel<T, E4M3>;
+  static std::atomic<bool> attr_set[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  if (!attr_set[dev].load()) {
+    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kResSlabMax));
+    if (e != cudaSuccess) return e;
+    attr_set[dev].store(true);
+  }
+  auto* barrier = static_cast<uint32_t*>(ws);
+  auto* partials = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + kQuantPartialsOffset);
+  cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(uint32_t), st);
+  note_launch();
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(kResThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kernel, static_cast<const T*>(x), n, vpc, barrier, partials, scale_out,
+                         static_cast<uint8_t*>(out), error_word_ptr());
+  note_launch();
+  *used = true;
+  return e;
+}
+
+template <typename T, bool E4M3>
+cudaError_t quant_any_t(const void* x, int64_t n, float* scale_out, void* out, void* ws, size_t ws_bytes,
+                        cudaStream_t st) {
+  bool used = false;
+  cudaError_t e = quant_res_t<T, E4M3>(x, n, scale_out, out, ws, ws_bytes, st, &used);
+  if (e != cudaSuccess || used) return e;
+  return quant_dyn_t<T, E4M3>(x, n, scale_out, out, ws, ws_bytes, st);
+}
 }  // namespace
 
 size_t quantize_dynamic_workspace_bytes() {
@@ -520,12 +727,12 @@ cudaError_t quantize_dynamic_launch(const void* x, int64_t n, int x_dtype, float
                                     void* ws, size_t ws_bytes, cudaStream_t st) {
   const bool e4 = (out_dtype == E4M3);
   switch (x_dtype) {
-    case F16: return e4 ? quant_dyn_t<__half, true>(x, n, scale_out, out, ws, ws_bytes, st)
-                        : quant_dyn_t<__half, false>(x, n, scale_out, out, ws, ws_bytes, st);
-    case BF16: return e4 ? quant_dyn_t<__nv_bfloat16, true>(x, n, scale_out, out, ws, ws_bytes, st)
-                         : quant_dyn_t<__nv_bfloat16, false>(x, n, scale_out, out, ws, ws_bytes, st);
-    default: return e4 ? quant_dyn_t<float, true>(x, n, scale_out, out, ws, ws_bytes, st)
-                       : quant_dyn_t<float, false>(x, n, scale_out, out, ws, ws_bytes, st);
+    case F16: return e4 ? quant_any_t<__half, true>(x, n, scale_out, out, ws, ws_bytes, st)
+                        : quant_any_t<__half, false>(x, n, scale_out, out, ws, ws_bytes, st);
+    case BF16: return e4 ? quant_any_t<__nv_bfloat16, true>(x, n, scale_out, out, ws, ws_bytes, st)
+                         : quant_any_t<__nv_bfloat16, false>(x, n, scale_out, out, ws, ws_bytes, st);
+    default: return e4 ? quant_any_t<float, true>(x, n, scale_out, out, ws, ws_bytes, st)
+                       : quant_any_t<float, false>(x, n, scale_out, out, ws, ws_bytes, st);
   }
 }
 

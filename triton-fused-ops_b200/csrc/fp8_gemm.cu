@@ -105,29 +105,74 @@ __global__ void __launch_bounds__(256) prep_rows_s8_sum_kernel(const uint8_t* __
 }
 
 // Columns: dst[k, n] = src[k, n] ^ 0x80 for a [K, N] matrix (N % 16 == 0) and
-// sums[n] += the column's int8 values over this block's K range (sums must be
-// zeroed first; integer atomics keep the result exact and order-independent).
-__global__ void __launch_bounds__(64) prep_cols_s8_sum_kernel(const uint8_t* __restrict__ src, int64_t K, int64_t N,
-                                                               int64_t k_per_block, int8_t* __restrict__ dst,
-                                                               int32_t* __restrict__ sums) {
+// sums[n] += the column's int8 values over this CTA's K range (sums zeroed
+// first; integer atomics keep the result exact and order-independent).
+// A CTA covers kColChunks 16-byte column chunks (1024 columns) and
+// kColGroups * kColRows rows; thread (group g, chunk c) reads rows g, g + G, ...
+// so a warp reads 512 contiguous bytes of one row, with kColUnroll loads in
+// flight. Raw codes are summed two bytes per 32-bit word in 16-bit lanes (at
+// most kColRows * 255 per lane), the groups are combined in shared memory,
+// and each column receives one atomic per CTA.
+constexpr int kColChunks = 64, kColGroups = 8, kColRows = 16, kColUnroll = 8;
+constexpr int kColThreads = kColChunks * kColGroups;
+static_assert(kColRows * 255 < 65536 && kColRows % kColUnroll == 0, "16-bit lane sums");
+
+__global__ void __launch_bounds__(kColThreads) prep_cols_s8_sum_kernel(const uint8_t* __restrict__ src, int64_t K,
+                                                                        int64_t N, int8_t* __restrict__ dst,
+                                                                        int32_t* __restrict__ sums) {
+  __shared__ int32_t part[kColGroups][kColChunks * 17];  // 17-word stride: no bank conflicts
+  const int cx = threadIdx.x % kColChunks, g = threadIdx.x / kColChunks;
   const int64_t chunks = N / 16;
-  const int64_t c = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (c >= chunks) return;
-  const int64_t k0 = static_cast<int64_t>(blockIdx.y) * k_per_block;
-  const int64_t k1 = min(K, k0 + k_per_block);
-  int acc[16];
+  const int64_t c = static_cast<int64_t>(blockIdx.x) * kColChunks + cx;
+  const int64_t k0 = static_cast<int64_t>(blockIdx.y) * (kColGroups * kColRows) + g;
+  uint32_t even[4] = {0u, 0u, 0u, 0u}, odd[4] = {0u, 0u, 0u, 0u};
+  int rows = 0;
+  if (c < chunks) {
+#pragma unroll 1
+    for (int i0 = 0; i0 < kColRows; i0 += kColUnroll) {
+      uint4 u[kColUnroll];
 #pragma unroll
-  for (int j = 0; j < 16; ++j) acc[j] = 0;
-  for (int64_t k = k0; k < k1; ++k) {
-    uint4 u = __ldcs(reinterpret_cast<const uint4*>(src + k * N) + c);
-    u.x ^= 0x80808080u; u.y ^= 0x80808080u; u.z ^= 0x80808080u; u.w ^= 0x80808080u;
-    reinterpret_cast<uint4*>(dst + k * N)[c] = u;
-    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+      for (int i = 0; i < kColUnroll; ++i) {
+        const int64_t k = k0 + static_cast<int64_t>(i0 + i) * kColGroups;
+        if (k < K) u[i] = __ldcs(reinterpret_cast<const uint4*>(src + k * N) + c);
+      }
 #pragma unroll
-    for (int j = 0; j < 16; ++j) acc[j] += static_cast<int8_t>((w[j >> 2] >> (8 * (j & 3))) & 0xffu);
+      for (int i = 0; i < kColUnroll; ++i) {
+        const int64_t k = k0 + static_cast<int64_t>(i0 + i) * kColGroups;
+        if (k < K) {
+          const uint32_t w[4] = {u[i].x, u[i].y, u[i].z, u[i].w};
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            even[q] += w[q] & 0x00FF00FFu;
+            odd[q] += (w[q] >> 8) & 0x00FF00FFu;
+          }
+          reinterpret_cast<uint4*>(dst + k * N)[c] =
+              make_uint4(w[0] ^ 0x80808080u, w[1] ^ 0x80808080u, w[2] ^ 0x80808080u, w[3] ^ 0x80808080u);
+          ++rows;
+        }
+      }
+    }
   }
+  // word q holds columns 4q .. 4q+3 in bytes 0..3: bytes 0, 2 in `even`, 1, 3 in `odd`
+  int32_t* mine = &part[g][cx * 17];
+  const int32_t bias = 128 * rows;
 #pragma unroll
-  for (int j = 0; j < 16; ++j) atomicAdd(sums + c * 16 + j, acc[j]);
+  for (int q = 0; q < 4; ++q) {
+    mine[4 * q + 0] = static_cast<int32_t>(even[q] & 0xFFFFu) - bias;
+    mine[4 * q + 1] = static_cast<int32_t>(odd[q] & 0xFFFFu) - bias;
+    mine[4 * q + 2] = static_cast<int32_t>(even[q] >> 16) - bias;
+    mine[4 * q + 3] = static_cast<int32_t>(odd[q] >> 16) - bias;
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < kColChunks * 16; j += kColThreads) {
+    const int64_t col = static_cast<int64_t>(blockIdx.x) * kColChunks * 16 + j;
+    if (col < N) {
+      int32_t t = 0;
+#pragma unroll
+      for (int gg = 0; gg < kColGroups; ++gg) t += part[gg][(j >> 4) * 17 + (j & 15)];
+      atomicAdd(sums + col, t);
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -442,11 +487,11 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
       e = cudaMemsetAsync(sums, 0, static_cast<size_t>(g.N) * 4, st);
       note_launch();
       if (e != cudaSuccess) return e;
-      // 64 column chunks (1024 columns) x 32 K rows per CTA: >= 8 CTAs per SM for 4096 x 4096
       const int64_t chunks = g.N / 16;
-      const int64_t kpb = 32;
-      dim3 grid(static_cast<unsigned>((chunks + 63) / 64), static_cast<unsigned>((g.K + kpb - 1) / kpb));
-      prep_cols_s8_sum_kernel<<<grid, 64, 0, st>>>(b, g.K, g.N, kpb, db, sums);
+      const int64_t rows_per_cta = kColGroups * kColRows;
+      dim3 grid(static_cast<unsigned>((chunks + kColChunks - 1) / kColChunks),
+                static_cast<unsigned>((g.K + rows_per_cta - 1) / rows_per_cta));
+      prep_cols_s8_sum_kernel<<<grid, kColThreads, 0, st>>>(b, g.K, g.N, db, sums);
       note_launch();
     } else {
       const int grid = static_cast<int>(std::min<int64_t>((g.N + 7) / 8, num_sms() * 8));
