@@ -694,7 +694,7 @@ def run_profile_op(args):
         cos, sin = rope_tables(seq, D, dev)
         fn = lambda: triton_ops.fused_rmsnorm_rope(x, w, cos, sin)
     elif op == "fp8_gemm":
-        m = {"small": 128, "config4": 1024, "config3": 8192, "prefill": 8192}[shape]
+        m = {"m16": 16, "small": 128, "config4": 1024, "config3": 8192, "prefill": 8192}[shape]
         qd = torch.float8_e4m3fn if args.profile_dtype == "e4m3" else torch.uint8
         qa, sa = triton_ops.quantize_fp8(torch.randn(m, H, device=dev, generator=g).half(), dtype=qd)
         qb, sb = triton_ops.quantize_fp8(torch.randn(H, H, device=dev, generator=g).half(), dtype=qd)

@@ -33,26 +33,34 @@ int gemm_resident_units(const void* kernel, size_t smem, int cg);
 // environment sets TFO_B200_PAIR_MMA=0 (read once per process).
 bool pair_mma_enabled();
 
+// Launches a GEMM kernel (192 threads) on `grid` CTAs as clusters of
+// `cluster` consecutive CTAs (1 = no cluster).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_gemm_grid(void (*kernel)(KArgs...), int grid, int cluster, size_t smem, cudaStream_t st,
+                             Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (cluster > 1) {
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = (cluster > 1) ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Launches a persistent GEMM kernel: `units` work units (see above) of 192
 // threads, as clusters of two CTAs when cg == 2.
 template <typename... KArgs, typename... Args>
 cudaError_t launch_gemm_units(void (*kernel)(KArgs...), int cg, int units, size_t smem, cudaStream_t st,
                               Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(units * cg));
-  cfg.blockDim = dim3(192);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  if (cg == 2) {
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = 2;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = (cg == 2) ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  return launch_gemm_grid(kernel, units * cg, cg, smem, st, std::forward<Args>(args)...);
 }
 
 struct RmsNormRopeArgs {

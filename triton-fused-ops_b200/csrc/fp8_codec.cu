@@ -60,16 +60,28 @@ __device__ __forceinline__ uint32_t ref_encode(float c) {
 // exact for |y| < 2^22). The low byte is rint(y) mod 256, so the code
 // rint(y) + 128 is that byte XOR 0x80.
 __device__ __forceinline__ uint32_t ref_encode4_in_range(float c0, float c1, float c2, float c3) {
-  auto kbits = [](float c) -> uint32_t {
-    constexpr float kInv7 = 0.142857142857142857f;
-    const float q0 = __fmul_rn(c, kInv7);
-    const float r = __fmaf_rn(-q0, 7.0f, c);
-    const float q = __fmaf_rn(r, kInv7, q0);
-    return __float_as_uint(__fadd_rn(__fmul_rn(q, 1.984375f), 12582912.0f));
+  // RN(c / 7) on two packed lanes at a time. The last multiply and the
+  // rounding addition stay scalar: __fmul_rn / __fadd_rn are never contracted
+  // into an fma, while a packed mul followed by a packed add was seen to be
+  // (which skips the rounding of q * 1.984375 and breaks exact ties).
+  const F2 inv7 = f2(0.142857142857142857f, 0.142857142857142857f), m7 = f2(-7.0f, -7.0f);
+  auto kbits2 = [&](F2 c) -> F2 {
+    const F2 q0 = mul2(c, inv7);
+    const F2 r = fma2(q0, m7, c);  // c - 7 q0, exact
+    const F2 q = fma2(r, inv7, q0);
+    return f2(__fadd_rn(__fmul_rn(q.x, 1.984375f), 12582912.0f), __fadd_rn(__fmul_rn(q.y, 1.984375f), 12582912.0f));
   };
-  const uint32_t lo = __byte_perm(kbits(c0), kbits(c1), 0x0040);
-  const uint32_t hi = __byte_perm(kbits(c2), kbits(c3), 0x0040);
+  const F2 a = kbits2(f2(c0, c1)), b = kbits2(f2(c2, c3));
+  const uint32_t lo = __byte_perm(__float_as_uint(a.x), __float_as_uint(a.y), 0x0040);
+  const uint32_t hi = __byte_perm(__float_as_uint(b.x), __float_as_uint(b.y), 0x0040);
   return __byte_perm(lo, hi, 0x5410) ^ 0x80808080u;
+}
+
+// As above for x0..x3 * s (the scale product rounded first, also packed).
+__device__ __forceinline__ uint32_t ref_encode4_in_range_scaled(const float* x, float s) {
+  const F2 ss = f2(s, s);
+  const F2 c01 = mul2(f2(x[0], x[1]), ss), c23 = mul2(f2(x[2], x[3]), ss);
+  return ref_encode4_in_range(c01.x, c01.y, c23.x, c23.y);
 }
 
 // ---- 16 elements at a time -------------------------------------------------
@@ -186,7 +198,7 @@ __device__ __forceinline__ void encode_share(const T* __restrict__ x, int64_t n,
                                                    __NV_SATFINITE, __NV_E4M3);
       return lo | (hi << 16);
     } else if constexpr (IN_RANGE) {
-      return ref_encode4_in_range(__fmul_rn(f[0], s), __fmul_rn(f[1], s), __fmul_rn(f[2], s), __fmul_rn(f[3], s));
+      return ref_encode4_in_range_scaled(f, s);
     } else {
       return enc1(f[0]) | (enc1(f[1]) << 8) | (enc1(f[2]) << 16) | (enc1(f[3]) << 24);
     }
@@ -348,7 +360,7 @@ __global__ void __launch_bounds__(kQuantThreads, 2)
 // encodes its slab from shared memory. HBM sees one read of x and one write
 // of the codes. 16-byte vectors; the last CTA also covers the n % 16 tail
 // elements from global memory.
-constexpr int kResThreads = 512;
+constexpr int kResThreads = 1024;
 constexpr int kResPieces = 8;
 constexpr size_t kResSlabMax = 227 * 1024 - 1024;
 
@@ -457,9 +469,7 @@ __global__ void __launch_bounds__(kResThreads, 1)
       }
     } else if (in_range) {
 #pragma unroll
-      for (int h = 0; h < EV / 4; ++h)
-        w[h] = ref_encode4_in_range(__fmul_rn(f[4 * h], s), __fmul_rn(f[4 * h + 1], s), __fmul_rn(f[4 * h + 2], s),
-                                    __fmul_rn(f[4 * h + 3], s));
+      for (int h = 0; h < EV / 4; ++h) w[h] = ref_encode4_in_range_scaled(f + 4 * h, s);
     } else {
 #pragma unroll
       for (int h = 0; h < EV / 4; ++h)

@@ -202,6 +202,17 @@ struct Fp8Epi {
   static __device__ __forceinline__ State init(const Params& p) {
     return {static_cast<float>(p.codec_k / (static_cast<double>(__ldg(p.sa)) * __ldg(p.sb)))};
   }
+  // cluster K split: sum of two slices' raw accumulators (int32 wraps exactly;
+  // fp32 in slice order) and the parameters of the final epilogue call
+  static __device__ __forceinline__ uint32_t add_partial(uint32_t a, uint32_t b) {
+    if constexpr (INT_ACC) return a + b;
+    else return __float_as_uint(__uint_as_float(a) + __uint_as_float(b));
+  }
+  static __device__ __forceinline__ Params final_params(const Params& p) {
+    Params q = p;
+    q.partial = nullptr;
+    return q;
+  }
   __device__ __forceinline__ void operator()(const Params& p, const State& st, const uint32_t (&r)[1][16], int row,
                                              int col0, int M, int N, int split) const {
     if (row >= M || col0 >= N) return;
@@ -302,6 +313,7 @@ struct Fp8Plan {
   bool b_mn;            // B read MN-major from [K, N]
   size_t off_a, off_b, off_sum, off_part, bytes;
   int bn, cg, splits;
+  bool ksplit_cluster;  // K slices of a tile reduced inside one cluster (no partials, no finalize)
 };
 
 // Tile shape: 256-column tiles, as two-CTA 256 x 256 tiles when M has more
@@ -318,6 +330,7 @@ void pick_tiles(int64_t M, int64_t N, int64_t Kp, Fp8Plan& p) {
   const int64_t num_k = (Kp + 127) / 128;
   p.splits = 1;
   if (tiles < units / 2) p.splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_k / 4, units / tiles)));
+  p.ksplit_cluster = (p.splits > 1 && p.splits <= 8 && p.cg == 1 && p.bn == 128);
 }
 
 Fp8Plan plan_fp8(const Fp8GemmArgs& g, bool assume_aligned) {
@@ -352,7 +365,7 @@ Fp8Plan plan_fp8(const Fp8GemmArgs& g, bool assume_aligned) {
   }
   pick_tiles(g.M, g.N, p.Kp, p);
   p.off_part = off;
-  if (p.splits > 1) off += round_up(static_cast<int64_t>(p.splits) * g.M * g.N * 4, 256);
+  if (p.splits > 1 && !p.ksplit_cluster) off += round_up(static_cast<int64_t>(p.splits) * g.M * g.N * 4, 256);
   p.bytes = off;
   return p;
 }
@@ -373,6 +386,22 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
                           al16(g.c) && (g.N * sizeof(TO)) % 16 == 0, corr_row, corr_col,
                           p.splits > 1 ? partial : nullptr};
   const int64_t work = ((g.M + L::PAIR_M - 1) / L::PAIR_M) * ((g.N + BN - 1) / BN) * p.splits;
+  if constexpr (CG == 1 && BN == 128) {
+    if (p.ksplit_cluster) {
+      // one CTA per (tile, K slice); the slices of a tile form one cluster
+      using LK = GemmLayout<BN, 1, kStages, 1, true>;
+      auto kk = umma_gemm_kernel<KIND, BN, 1, kStages, Epi, B_MN, 1, true>;
+      if (gemm_resident_units(reinterpret_cast<const void*>(kk), LK::SMEM_BYTES, 1) <= 0)
+        return cudaErrorInvalidConfiguration;
+      typename Epi::Params epk = ep;
+      epk.partial = nullptr;
+      cudaError_t ek = launch_gemm_grid(kk, static_cast<int>(work), p.splits, LK::SMEM_BYTES, st, ta, tb, tb,
+                                        static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(p.Kp),
+                                        kGroupM, idesc, epk, error_word_ptr(), p.splits);
+      note_launch();
+      return ek;
+    }
+  }
   const int units = static_cast<int>(std::min<int64_t>(work, resident));
   cudaError_t e = launch_gemm_units(kern, CG, units, L::SMEM_BYTES, st, ta, tb, tb, static_cast<int>(g.M),
                                     static_cast<int>(g.N), static_cast<int>(p.Kp), kGroupM, idesc, ep,

@@ -48,7 +48,7 @@ struct TileSched {
 
 // Per-CTA shared-memory layout. The UMMA is M = 128 * CG by N = NUM_B *
 // BLOCK_N; each CTA stages 128 rows of A and N / CG rows of B per K block.
-template <int BLOCK_N, int NUM_B, int STAGES, int CG = 1>
+template <int BLOCK_N, int NUM_B, int STAGES, int CG = 1, bool KSPLIT = false>
 struct GemmLayout {
   static constexpr int BM = 128;             // A rows (and accumulator lanes) per CTA
   static constexpr int PAIR_M = BM * CG;     // rows per tile
@@ -64,9 +64,31 @@ struct GemmLayout {
   static_assert(BLOCK_N % 16 == 0 && BLOCK_N >= 16 && N_MMA <= 256, "UMMA N");
   static_assert(CG == 1 || (B_ROWS % 128 == 0 && (NUM_B == 1 || B_ROWS == BLOCK_N)),
                 "pair MMA: each CTA stages whole 128-row B boxes (one operand each when NUM_B == 2)");
-  // dynamic shared memory: ring + barriers + 1 KB for manual alignment
-  static constexpr size_t SMEM_BYTES = static_cast<size_t>(STAGES) * STAGE_BYTES + 256 + 1024;
+  static_assert(!KSPLIT || (CG == 1 && NUM_B == 1), "cluster K split: one CTA per MMA, one B operand");
+  // cluster K split: the raw accumulator tile, read by the cluster's other CTAs
+  static constexpr int RED_BYTES = KSPLIT ? BM * N_MMA * 4 : 0;
+  static constexpr int RED_OFFSET = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFFSET = RED_OFFSET + RED_BYTES;
+  // dynamic shared memory: ring + reduction tile + barriers + 1 KB for manual alignment
+  static constexpr size_t SMEM_BYTES = static_cast<size_t>(BAR_OFFSET) + 256 + 1024;
 };
+
+// Address of 16-byte vector `v` of accumulator row `row` in the reduction
+// tile (N_MMA / 4 vectors per row, XOR-swizzled by row so that the 32 rows of
+// a warp spread over all banks).
+template <int VECS_PER_ROW>
+__device__ __forceinline__ int red_vec_index(int row, int v) {
+  return row * VECS_PER_ROW + (v ^ (row & 7));
+}
+
+__device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t cluster_addr) {
+  uint4 r;
+  asm volatile("ld.shared::cluster.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return r;
+}
 
 // Waits for `parity` on `bar`, giving up when the CTA abort flag is raised or
 // the budget runs out (then sets the error bit and raises the flag).
@@ -108,21 +130,31 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 // the even CTA's `full` barrier. The even CTA issues the M = 256 MMAs and
 // commits to the `empty` / `tfull` barriers of both CTAs; the epilogue warps
 // of both CTAs release the accumulator on the even CTA's `tempty` barrier.
-template <MmaKind KIND, int BLOCK_N, int NUM_B, int STAGES, class Epi, bool B_MN = false, int CG = 1>
+//
+// KSPLIT: the k_splits K slices of a tile run as one cluster of k_splits CTAs
+// (one work item per CTA, grid = tiles x k_splits). Each CTA leaves its raw
+// accumulator tile in shared memory; after a cluster barrier CTA r sums rows
+// [r * 128 / k_splits, +128 / k_splits) over the cluster's tiles in slice
+// order (through distributed shared memory) and runs the epilogue on the sums
+// (Epi must provide add_partial and final_params); a second cluster barrier
+// keeps every tile readable until all CTAs are done.
+template <MmaKind KIND, int BLOCK_N, int NUM_B, int STAGES, class Epi, bool B_MN = false, int CG = 1,
+          bool KSPLIT = false>
 __global__ void __launch_bounds__(192, 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
                      const __grid_constant__ CUtensorMap tmap_b1, int M, int N, int K, int group_m, uint32_t idesc,
                      const typename Epi::Params ep, uint32_t* err, int k_splits) {
   static_assert(!B_MN || (NUM_B == 1 && KindTraits<KIND>::ELEM == 1 && BLOCK_N % 128 == 0),
                 "MN-major B: 8-bit operands, one B operand, BLOCK_N a multiple of 128");
-  using L = GemmLayout<BLOCK_N, NUM_B, STAGES, CG>;
+  using L = GemmLayout<BLOCK_N, NUM_B, STAGES, CG, KSPLIT>;
   constexpr int KB_ELEMS = 128 / KindTraits<KIND>::ELEM;
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + STAGES * L::A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * L::STAGE_BYTES);
+  uint4* red_tile = reinterpret_cast<uint4*>(smem + L::RED_OFFSET);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -297,6 +329,24 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t base = tmem_base + lane_addr + acc * L::ACC_COLS;
       // Two register sets: the TMEM load of the next 16 columns is in flight
       // while the current ones are converted and stored.
+      if constexpr (KSPLIT) {
+        // raw accumulators to the reduction tile (row = this thread's TMEM lane)
+        const int trow = sub * 32 + lane;
+#pragma unroll 1
+        for (int c = 0; c < BLOCK_N; c += 16) {
+          uint32_t r[16];
+          tmem_ld16(base + c, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            red_tile[red_vec_index<L::N_MMA / 4>(trow, c / 4 + q)] =
+                make_uint4(r[4 * q], r[4 * q + 1], r[4 * q + 2], r[4 * q + 3]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        continue;
+      }
       static_assert(BLOCK_N % 32 == 0, "epilogue walks 32 columns per iteration");
       uint32_t ra[NUM_B][16], rb[NUM_B][16];
 #pragma unroll
@@ -325,6 +375,37 @@ __global__ void __launch_bounds__(192, 1)
   }
 
   __syncthreads();
+  if constexpr (KSPLIT) {
+    cluster_sync();  // every slice's tile is in shared memory
+    if (warp >= 2) {
+      const typename Epi::State est = Epi::init(ep);
+      const typename Epi::Params epf = Epi::final_params(ep);
+      const Work wk = work(blockIdx.x);
+      const int rows_per = (L::BM + k_splits - 1) / k_splits;
+      const int r0 = static_cast<int>(cluster_ctarank()) * rows_per;
+      const int nrows = max(0, min(L::BM, r0 + rows_per) - r0);
+      constexpr int CHUNKS = BLOCK_N / 16;
+      const uint32_t tile_base = smem_u32(red_tile);
+      for (int u = threadIdx.x - 64; u < nrows * CHUNKS; u += 128) {
+        const int trow = r0 + u / CHUNKS, c = (u % CHUNKS) * 16;
+        const int row = wk.m_blk * L::PAIR_M + trow;
+        if (row >= M) continue;
+        uint32_t sum[1][16];
+        for (int sl = 0; sl < k_splits; ++sl) {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const uint32_t off = static_cast<uint32_t>(red_vec_index<L::N_MMA / 4>(trow, c / 4 + q)) * 16u;
+            const uint4 v = ld_dsmem_v4(mapa_shared(tile_base + off, static_cast<uint32_t>(sl)));
+            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) sum[0][4 * q + j] = sl == 0 ? w[j] : Epi::add_partial(sum[0][4 * q + j], w[j]);
+          }
+        }
+        Epi{}(epf, est, sum, row, wk.n_blk * BLOCK_N + c, M, N, 0);
+      }
+    }
+    cluster_sync();  // no CTA leaves while the others may still read its tile
+  }
   if constexpr (CG == 2) cluster_sync();  // no CTA leaves while its pair may still touch its memory
   if (warp == 1) {
     __syncwarp();
