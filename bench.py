@@ -419,6 +419,29 @@ def components(peaks, flush_buf):
     out["library_scaled_mm_e4m3_Mx4096x4096"] = lib8
     del bs, bs8, bs8_nk
 
+    # fused RMSNorm+RoPE -> 8-bit codes at the prefill shape [8, 8192, 4096] fp16,
+    # dynamic and given scale, and the two ops run separately; GB/s counts the
+    # op's own input and output (8 KB of x read + 4 KB of codes written per row)
+    xq = [torch.randn(8, 8192, 4096, device=dev, generator=g).half() for _ in range(2)]
+    wq = (1 + 0.1 * torch.randn(4096, device=dev, generator=g)).half()
+    cq, sq = rope_tables(8192, 64, dev)
+    rows = 8 * 8192
+    two = torch.tensor(2.0, device=dev)
+    fq = {}
+    us, err = time_graph([lambda x=x: triton_ops.fused_rmsnorm_rope_quantize(x, wq, cq, sq) for x in xq], reps=5)
+    fq["dynamic_scale"] = entry(us, err, None, nbytes=rows * (8192 + 4096))
+    us, err = time_graph([lambda x=x: triton_ops.fused_rmsnorm_rope_quantize(x, wq, cq, sq, scale=two) for x in xq],
+                         reps=5)
+    fq["given_scale"] = entry(us, err, None, nbytes=rows * (8192 + 4096))
+    us, err = time_graph([lambda x=x: triton_ops.quantize_fp8(triton_ops.fused_rmsnorm_rope(x, wq, cq, sq))
+                          for x in xq], reps=5)
+    fq["unfused_dynamic"] = {"us": us, "graph_error": err}
+    us, err = time_graph([lambda x=x: triton_ops.quantize_fp8(triton_ops.fused_rmsnorm_rope(x, wq, cq, sq), two)
+                          for x in xq], reps=5)
+    fq["unfused_given_scale"] = {"us": us, "graph_error": err}
+    out["rmsnorm_rope_quantize_8x8192x4096"] = fq
+    del xq
+
     # gated MLP at [2, 1024, 4096] x [11264, 4096] (weights alone exceed L2)
     xm = [torch.randn(2, 1024, 4096, device=dev, generator=g).half() for _ in range(2)]
     wg = (0.02 * torch.randn(11264, 4096, device=dev, generator=g)).half()

@@ -102,6 +102,26 @@ TFO_API int tfo_rmsnorm_rope(const void* x, const void* weight, const void* cos,
                      int64_t cs_stride_dim, double eps, int x_dtype, int w_dtype, int cos_dtype, int sin_dtype,
                      void* stream);
 
+/* RMSNorm + RoPE as tfo_rmsnorm_rope, with the output as 8-bit codes
+ * (code_dtype TFO_DTYPE_U8: the reference codec; TFO_DTYPE_E4M3): codes and
+ * scale equal tfo_fp8_quantize of the tfo_rmsnorm_rope output byte for byte.
+ * The rows are written to the workspace and encoded from there. With scale
+ * == NULL (dynamic per-tensor scale 448 / max|output|, written to scale_out)
+ * the row pass also records one max per CTA when tfo_rmsnorm_rope runs its
+ * warp-per-row kernel on the shape (tfo_select_tile(TFO_OP_RMSNORM_ROPE,
+ * batch * seq_len, ...) kernel 2, 16-byte-aligned x, one cos/sin dtype), so
+ * the encode pass derives the scale without a separate read of the rows.
+ * Workspace: tfo_rmsnorm_rope_quantize_workspace_bytes (the rows plus a few
+ * KB). No counterpart in the reference: this is the RMSNorm+RoPE -> FP8
+ * fusion its roadmap lists for FusedRMSNormRoPE -> FP8Linear chains. */
+TFO_API size_t tfo_rmsnorm_rope_quantize_workspace_bytes(int64_t batch, int64_t seq_len, int64_t hidden, int x_dtype);
+TFO_API int tfo_rmsnorm_rope_quantize(const void* x, const void* weight, const void* cos, const void* sin, void* codes,
+                                      int64_t batch, int64_t seq_len, int64_t hidden, int64_t head_dim,
+                                      int64_t num_heads, int64_t cs_stride_seq, int64_t cs_stride_dim, double eps,
+                                      int x_dtype, int w_dtype, int cos_dtype, int sin_dtype, const float* scale,
+                                      float* scale_out, int code_dtype, void* workspace, size_t workspace_bytes,
+                                      void* stream);
+
 /* Bytes of workspace needed by the dynamic-scale codec calls for numel elements. */
 TFO_API size_t tfo_fp8_scale_workspace_bytes(int64_t numel);
 

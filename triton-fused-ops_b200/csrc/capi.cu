@@ -201,6 +201,82 @@ int tfo_rmsnorm_rope(const void* x, const void* weight, const void* cos, const v
 
 size_t tfo_fp8_scale_workspace_bytes(int64_t numel) { return scale_workspace_bytes(numel); }
 
+size_t tfo_rmsnorm_rope_quantize_workspace_bytes(int64_t batch, int64_t seq_len, int64_t hidden, int x_dtype) {
+  // the rows, then the amax partials or the quantize's own workspace
+  const int64_t n = std::max<int64_t>(0, batch) * std::max<int64_t>(0, seq_len) * std::max<int64_t>(0, hidden);
+  const size_t y_bytes = (static_cast<size_t>(n) * (x_dtype == F32 ? 4 : 2) + 255) / 256 * 256;
+  const size_t parts = sizeof(uint32_t) * static_cast<size_t>(rmsnorm_rope_quant_max_parts());
+  return y_bytes + std::max(parts, scale_workspace_bytes(n));
+}
+
+int tfo_rmsnorm_rope_quantize(const void* x, const void* weight, const void* cos, const void* sin, void* codes,
+                              int64_t batch, int64_t seq_len, int64_t hidden, int64_t head_dim, int64_t num_heads,
+                              int64_t cs_stride_seq, int64_t cs_stride_dim, double eps, int x_dtype, int w_dtype,
+                              int cos_dtype, int sin_dtype, const float* scale, float* scale_out, int code_dtype,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  const char* fn = "tfo_rmsnorm_rope_quantize";
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(w_dtype) || !is_float_dtype(cos_dtype) ||
+      !is_float_dtype(sin_dtype))
+    return fail(TFO_ERR_DTYPE, std::string(fn) + ": dtypes must be f16, bf16 or f32");
+  if (code_dtype != U8 && code_dtype != E4M3) return fail(TFO_ERR_DTYPE, std::string(fn) + ": codes must be U8 or E4M3");
+  if (batch < 0 || seq_len < 0 || hidden <= 0 || head_dim <= 0 || num_heads < 0)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": negative or zero dimension");
+  if (head_dim % 2 != 0) return fail(TFO_ERR_INVALID, std::string(fn) + ": head_dim must be even");
+  if (num_heads * head_dim > hidden)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": num_heads * head_dim exceeds hidden");
+  if (hidden > (1 << 20) || seq_len > (1ll << 31) - 1)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": hidden or seq_len too large");
+  if (scale == nullptr && scale_out == nullptr)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": a dynamic scale needs scale_out");
+  const int64_t rows = batch * seq_len;
+  auto st = static_cast<cudaStream_t>(stream);
+  if (rows == 0) {
+    if (scale != nullptr) return TFO_OK;
+    // no elements: the dynamic scale of an empty tensor (1.0), from one zero partial
+    if (!workspace || workspace_bytes < sizeof(uint32_t))
+      return fail(TFO_ERR_INVALID, std::string(fn) + ": workspace too small");
+    uint32_t* parts = static_cast<uint32_t*>(workspace);
+    cudaError_t e = amax_partials_launch(x, 0, x_dtype, parts, 1, st);
+    if (e == cudaSuccess) e = finalize_scale_launch(parts, 1, scale_out, st);
+    return e == cudaSuccess ? TFO_OK : cuda_fail(e, fn);
+  }
+  if (!x || !weight || !cos || !sin || !codes) return fail(TFO_ERR_INVALID, std::string(fn) + ": NULL pointer");
+  if (!workspace || workspace_bytes < tfo_rmsnorm_rope_quantize_workspace_bytes(batch, seq_len, hidden, x_dtype))
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": workspace too small");
+  // rows in the workspace, then the 8-bit encode of the rows
+  const size_t y_bytes = (static_cast<size_t>(rows * hidden) * (x_dtype == F32 ? 4 : 2) + 255) / 256 * 256;
+  void* tail = static_cast<char*>(workspace) + y_bytes;
+  const size_t tail_bytes = workspace_bytes - y_bytes;
+  RmsNormRopeArgs a{x,         weight,    cos,           sin,           workspace, batch,
+                    seq_len,   hidden,    head_dim,      num_heads,     cs_stride_seq,
+                    cs_stride_dim, static_cast<float>(eps), x_dtype, w_dtype,  cos_dtype, sin_dtype};
+  cudaError_t e = cudaErrorNotSupported;
+  if (scale == nullptr) {
+    // dynamic scale: the row pass also records one max |row value| per CTA,
+    // and the encode kernel reduces those to the scale (no separate amax pass)
+    RowQuantArgs q{static_cast<uint32_t*>(tail)};
+    int nparts = 0;
+    e = rmsnorm_rope_quant_launch(a, 3, q, &nparts, st);
+    if (e == cudaSuccess)
+      e = encode_launch(workspace, rows * hidden, x_dtype, nullptr, q.parts_out, nparts, scale_out, codes, code_dtype,
+                        st);
+  }
+  if (e == cudaErrorNotSupported) {
+    (void)cudaGetLastError();
+    e = rmsnorm_rope_launch(a, st);
+    if (e == cudaSuccess) {
+      e = (scale == nullptr)
+              ? quantize_dynamic_launch(workspace, rows * hidden, x_dtype, scale_out, codes, code_dtype, tail, tail_bytes,
+                                        st)
+              : encode_launch(workspace, rows * hidden, x_dtype, scale, nullptr, 0, nullptr, codes, code_dtype, st);
+    }
+  }
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return TFO_OK;
+}
+
+
+
 int tfo_select_tile(int op, int64_t M, int64_t N, int64_t K, int aux, int32_t* out, int n_out) {
   if (!out || n_out < 0) return fail(TFO_ERR_INVALID, "tfo_select_tile: NULL output");
   if (M < 0 || N < 0 || K < 0) return fail(TFO_ERR_INVALID, "tfo_select_tile: negative size");

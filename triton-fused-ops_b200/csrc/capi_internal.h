@@ -75,6 +75,19 @@ struct RmsNormRopeArgs {
   int x_dtype, w_dtype, cos_dtype, sin_dtype;
 };
 cudaError_t rmsnorm_rope_launch(const RmsNormRopeArgs& a, cudaStream_t st);
+// Extra output of the warp-per-row RMSNorm+RoPE kernel for a fused quantize:
+// one max |output value| per CTA.
+struct RowQuantArgs {
+  uint32_t* parts_out;
+};
+// RMSNorm+RoPE rows to a.out plus one amax partial per CTA to q.parts_out
+// (mode 3; *nparts receives their count). Returns cudaErrorNotSupported unless
+// tfo_rmsnorm_rope would run its warp-per-row kernel on this shape (same
+// kernel, so the rows are bit-identical); the caller then runs the two ops.
+cudaError_t rmsnorm_rope_quant_launch(const RmsNormRopeArgs& a, int mode, const RowQuantArgs& q, int* nparts,
+                                      cudaStream_t st);
+// Upper bound on the amax partials of mode 3 (one per CTA).
+int rmsnorm_rope_quant_max_parts();
 // Launch choice of tfo_rmsnorm_rope (see rmsnorm_rope_plan in rmsnorm_rope.cu).
 struct RmsPlan {
   int kind;     // 0 generic, 1 CTA per row, 2 warp per row

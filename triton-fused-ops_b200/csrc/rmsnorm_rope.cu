@@ -17,6 +17,7 @@
 #include <type_traits>
 
 #include "capi_internal.h"
+#include "codec.cuh"
 #include "common.cuh"
 
 namespace tfo {
@@ -315,11 +316,14 @@ inline size_t vec_smem_bytes(int hidden, int row_bytes, int stages) {
 // At most 12 warps with 16 vectors per lane (row kept in 64 registers), 16 otherwise.
 constexpr int warp_rows_max_warps(int vpl) { return vpl >= 16 ? 12 : 16; }
 
-template <typename TX, typename TCS, bool FULLROT, int VPL>
+// MODE 0 stores the output rows; MODE 3 also writes one max |output value|
+// per CTA to q.parts_out (the amax partials of a dynamic-scale quantize of the
+// rows, so that no separate amax pass over the rows is needed).
+template <typename TX, typename TCS, bool FULLROT, int VPL, int MODE>
 __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope_warp_kernel(
     const TX* __restrict__ x, const void* __restrict__ w, const TCS* __restrict__ cosp, const TCS* __restrict__ sinp,
     TX* __restrict__ out, int64_t rows, int seq_len, int hidden, int head_dim, int rot_cols, int64_t cs_ss,
-    int64_t cs_sd, float eps, int w_dtype, int cs_stride, uint32_t* err) {
+    int64_t cs_sd, float eps, int w_dtype, int cs_stride, uint32_t* err, const RowQuantArgs q) {
   constexpr int E = Pack<TX>::E;
   constexpr bool kExactProducts = sizeof(TX) == 2 && sizeof(TCS) == 2;
   const int W = blockDim.x >> 5;
@@ -362,6 +366,16 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
   const int c_off = (first ? hi : hi - hv) * E;
   const int s_off = (first ? 2 * half : half) + c_off;
 
+  __shared__ uint32_t qred[32];
+  uint32_t amax_lanes = 0;  // MODE 3: max |output| bits (per 16-bit lane for 16-bit TX)
+
+  // Stores output vector g of row `row` (16 bytes of packed TX words) and, in
+  // MODE 3, folds it into the running max.
+  auto emit = [&](int64_t row_, int g, const uint32_t (&wd)[4]) {
+    __stcs(reinterpret_cast<uint4*>(out + row_ * hidden) + g, make_uint4(wd[0], wd[1], wd[2], wd[3]));
+    if constexpr (MODE == 3) amax_lanes = absmax_vec<TX>(amax_lanes, make_uint4(wd[0], wd[1], wd[2], wd[3]));
+  };
+
   uint32_t par = 0;
   int pos = static_cast<int>(gw % seq_len);
   const int pos_step = static_cast<int>(GW % seq_len);
@@ -399,7 +413,6 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
     __syncwarp();
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(hidden)), eps));
     const float rb = __frcp_rn(rms);
-    uint4* orow = reinterpret_cast<uint4*>(out + row * hidden);
     const float4* c4 = reinterpret_cast<const float4*>(cs_buf + c_off);
     const float4* s4 = reinterpret_cast<const float4*>(cs_buf + s_off);
 
@@ -450,9 +463,9 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
           }
           uint32_t ow[4];
           pack_vec<TX, E>(o, ow);
-          __stcs(orow + g, make_uint4(ow[0], ow[1], ow[2], ow[3]));
+          emit(row, g, ow);
         } else {
-          __stcs(orow + g, make_uint4(yw[0], yw[1], yw[2], yw[3]));
+          emit(row, g, yw);
         }
       }
     };
@@ -464,6 +477,10 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
     __syncwarp();  // cs_buf is rewritten for the next row
     pos += pos_step;
     if (pos >= seq_len) pos -= seq_len;
+  }
+  if constexpr (MODE == 3) {
+    const uint32_t b = block_max_u32(absmax_to_f32_bits<TX>(amax_lanes), qred);
+    if (threadIdx.x == 0) q.parts_out[blockIdx.x] = b;
   }
 }
 
@@ -549,21 +566,36 @@ cudaError_t launch_vec(const RmsNormRopeArgs& a, int threads, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-template <typename TX, typename TCS, bool FULLROT, int VPL>
-cudaError_t launch_warp_rows_t(const RmsNormRopeArgs& a, int warps, int cs_stride, size_t smem, cudaStream_t st) {
-  auto kern = rmsnorm_rope_warp_kernel<TX, TCS, FULLROT, VPL>;
+// One CTA per SM at most, `warps` rows in flight per CTA.
+inline int64_t warp_rows_grid(int64_t rows, int warps) {
+  return std::max<int64_t>(1, std::min<int64_t>((rows + warps - 1) / warps, num_sms()));
+}
+
+template <typename TX, typename TCS, bool FULLROT, int VPL, int MODE>
+cudaError_t launch_warp_rows_m(const RmsNormRopeArgs& a, int warps, int cs_stride, size_t smem, const RowQuantArgs& q,
+                               cudaStream_t st) {
+  auto kern = rmsnorm_rope_warp_kernel<TX, TCS, FULLROT, VPL, MODE>;
   cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   const int64_t rows = a.batch * a.seq_len;
-  const int64_t grid = std::max<int64_t>(1, std::min<int64_t>((rows + warps - 1) / warps, num_sms()));
+  const int64_t grid = warp_rows_grid(rows, warps);
   kern<<<static_cast<unsigned>(grid), warps * 32, smem, st>>>(
       static_cast<const TX*>(a.x), a.weight, static_cast<const TCS*>(a.cos), static_cast<const TCS*>(a.sin),
       static_cast<TX*>(a.out), rows, static_cast<int>(a.seq_len), static_cast<int>(a.hidden),
       static_cast<int>(a.head_dim), static_cast<int>(a.num_heads * a.head_dim), a.cs_stride_seq, a.cs_stride_dim,
-      a.eps, a.w_dtype, cs_stride, error_word_ptr());
+      a.eps, a.w_dtype, cs_stride, error_word_ptr(), q);
   note_launch();
   return cudaGetLastError();
+}
+
+template <typename TX, typename TCS, bool FULLROT, int VPL>
+cudaError_t launch_warp_rows_t(const RmsNormRopeArgs& a, int warps, int cs_stride, size_t smem, int mode,
+                               const RowQuantArgs& q, cudaStream_t st) {
+  switch (mode) {
+    case 3: return launch_warp_rows_m<TX, TCS, FULLROT, VPL, 3>(a, warps, cs_stride, smem, q, st);
+    default: return launch_warp_rows_m<TX, TCS, FULLROT, VPL, 0>(a, warps, cs_stride, smem, q, st);
+  }
 }
 
 // Warps per CTA (one CTA per SM, at most 16) so that the row buffers, the
@@ -573,7 +605,7 @@ inline int warp_rows_config(int64_t hidden, int64_t head_dim, int elem, int max_
   *cs_stride = static_cast<int>((3 * (head_dim / 2) + 3) / 4 * 4);
   const size_t fixed = 16 * 8 + static_cast<size_t>(hidden) * 4 + 128;
   const size_t per_warp = row_bytes + static_cast<size_t>(*cs_stride) * 4;
-  const size_t limit = 227 * 1024;
+  const size_t limit = 227 * 1024 - 256;  // room for the kernel's static shared memory
   if (fixed + 8 * per_warp > limit) return 0;
   const int warps = static_cast<int>(std::min<size_t>(max_warps, (limit - fixed) / per_warp));
   *smem = ((16 * 8 + (static_cast<size_t>(hidden) + warps * *cs_stride) * 4 + 127) / 128) * 128 + warps * row_bytes;
@@ -581,17 +613,20 @@ inline int warp_rows_config(int64_t hidden, int64_t head_dim, int elem, int max_
 }
 
 template <typename TX, typename TCS, int VPL>
-cudaError_t launch_warp_rows_v(const RmsNormRopeArgs& a, int warps, int cs_stride, size_t smem, cudaStream_t st) {
-  return (a.num_heads * a.head_dim == a.hidden) ? launch_warp_rows_t<TX, TCS, true, VPL>(a, warps, cs_stride, smem, st)
-                                                : launch_warp_rows_t<TX, TCS, false, VPL>(a, warps, cs_stride, smem, st);
+cudaError_t launch_warp_rows_v(const RmsNormRopeArgs& a, int warps, int cs_stride, size_t smem, int mode,
+                               const RowQuantArgs& q, cudaStream_t st) {
+  return (a.num_heads * a.head_dim == a.hidden)
+             ? launch_warp_rows_t<TX, TCS, true, VPL>(a, warps, cs_stride, smem, mode, q, st)
+             : launch_warp_rows_t<TX, TCS, false, VPL>(a, warps, cs_stride, smem, mode, q, st);
 }
 
 template <typename TX, typename TCS>
-cudaError_t launch_warp_rows(const RmsNormRopeArgs& a, int vpl, int warps, int cs_stride, size_t smem, cudaStream_t st) {
+cudaError_t launch_warp_rows(const RmsNormRopeArgs& a, int vpl, int warps, int cs_stride, size_t smem, int mode,
+                             const RowQuantArgs& q, cudaStream_t st) {
   switch (vpl) {
-    case 4: return launch_warp_rows_v<TX, TCS, 4>(a, warps, cs_stride, smem, st);
-    case 8: return launch_warp_rows_v<TX, TCS, 8>(a, warps, cs_stride, smem, st);
-    default: return launch_warp_rows_v<TX, TCS, 16>(a, warps, cs_stride, smem, st);
+    case 4: return launch_warp_rows_v<TX, TCS, 4>(a, warps, cs_stride, smem, mode, q, st);
+    case 8: return launch_warp_rows_v<TX, TCS, 8>(a, warps, cs_stride, smem, mode, q, st);
+    default: return launch_warp_rows_v<TX, TCS, 16>(a, warps, cs_stride, smem, mode, q, st);
   }
 }
 
@@ -606,14 +641,18 @@ cudaError_t launch_cta_vec(const RmsNormRopeArgs& a, const RmsPlan& p, cudaStrea
 }
 
 template <typename TX>
-cudaError_t dispatch_plan(const RmsNormRopeArgs& a, const RmsPlan& p, cudaStream_t st) {
-  if (p.kind == 2) {
-    switch (a.cos_dtype) {
-      case F16: return launch_warp_rows<TX, __half>(a, p.vec, p.threads, p.cs_stride, p.smem, st);
-      case BF16: return launch_warp_rows<TX, __nv_bfloat16>(a, p.vec, p.threads, p.cs_stride, p.smem, st);
-      default: return launch_warp_rows<TX, float>(a, p.vec, p.threads, p.cs_stride, p.smem, st);
-    }
+cudaError_t dispatch_warp_rows(const RmsNormRopeArgs& a, const RmsPlan& p, int mode, const RowQuantArgs& q,
+                               cudaStream_t st) {
+  switch (a.cos_dtype) {
+    case F16: return launch_warp_rows<TX, __half>(a, p.vec, p.threads, p.cs_stride, p.smem, mode, q, st);
+    case BF16: return launch_warp_rows<TX, __nv_bfloat16>(a, p.vec, p.threads, p.cs_stride, p.smem, mode, q, st);
+    default: return launch_warp_rows<TX, float>(a, p.vec, p.threads, p.cs_stride, p.smem, mode, q, st);
   }
+}
+
+template <typename TX>
+cudaError_t dispatch_plan(const RmsNormRopeArgs& a, const RmsPlan& p, cudaStream_t st) {
+  if (p.kind == 2) return dispatch_warp_rows<TX>(a, p, 0, RowQuantArgs{}, st);
   switch (a.cos_dtype) {
     case F16: return launch_cta_vec<TX, __half>(a, p, st);
     case BF16: return launch_cta_vec<TX, __nv_bfloat16>(a, p, st);
@@ -689,6 +728,24 @@ RmsPlan rmsnorm_rope_plan(int64_t rows, int64_t hidden, int64_t head_dim, int64_
   }
   return p;
 }
+
+cudaError_t rmsnorm_rope_quant_launch(const RmsNormRopeArgs& a, int mode, const RowQuantArgs& q, int* nparts,
+                                      cudaStream_t st) {
+  const int esz = (a.x_dtype == F32) ? 4 : 2;
+  const bool ok = aligned16(a.x) && aligned16(a.out) && a.cos_dtype == a.sin_dtype;
+  // only where tfo_rmsnorm_rope itself runs the warp-per-row kernel, so that the
+  // rows (and their rounding) are exactly those of the unfused op
+  const RmsPlan p = rmsnorm_rope_plan(a.batch * a.seq_len, a.hidden, a.head_dim, a.num_heads, esz, ok);
+  if (p.kind != 2) return cudaErrorNotSupported;
+  *nparts = static_cast<int>(warp_rows_grid(a.batch * a.seq_len, p.threads));
+  switch (a.x_dtype) {
+    case F16: return dispatch_warp_rows<__half>(a, p, mode, q, st);
+    case BF16: return dispatch_warp_rows<__nv_bfloat16>(a, p, mode, q, st);
+    default: return dispatch_warp_rows<float>(a, p, mode, q, st);
+  }
+}
+
+int rmsnorm_rope_quant_max_parts() { return num_sms(); }
 
 cudaError_t rmsnorm_rope_launch(const RmsNormRopeArgs& a, cudaStream_t st) {
   const int esz = (a.x_dtype == F32) ? 4 : 2;

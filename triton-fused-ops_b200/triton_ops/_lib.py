@@ -58,6 +58,12 @@ _SIGNATURES = {
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
          ctypes.c_double, _c_int, _c_int, _c_int, _c_int, _c_vp],
     ),
+    "tfo_rmsnorm_rope_quantize_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64, _c_int]),
+    "tfo_rmsnorm_rope_quantize": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64, _c_i64,
+         ctypes.c_double, _c_int, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_int, _c_vp, _c_size, _c_vp],
+    ),
     "tfo_fp8_scale_workspace_bytes": (_c_size, [_c_i64]),
     "tfo_fp8_compute_scale": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_size, _c_vp]),
     "tfo_fp8_quantize": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_size, _c_vp]),

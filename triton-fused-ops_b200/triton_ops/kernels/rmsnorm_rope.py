@@ -26,6 +26,9 @@ fused_rmsnorm_rope_kernel = NativeKernel(
 # to the fused entry point here.
 rmsnorm_kernel = NativeKernel("rmsnorm_kernel", "tfo_rmsnorm_rope", "RMSNorm (fused with RoPE here)")
 rope_kernel = NativeKernel("rope_kernel", "tfo_rmsnorm_rope", "RoPE (fused with RMSNorm here)")
+fused_rmsnorm_rope_quantize_kernel = NativeKernel(
+    "fused_rmsnorm_rope_quantize_kernel", "tfo_rmsnorm_rope_quantize", "RMSNorm + RoPE rows with amax partials -> 8-bit encode"
+)
 
 
 def fused_rmsnorm_rope(
@@ -77,6 +80,75 @@ def fused_rmsnorm_rope(
         _lib.stream_of(x),
     )
     return out
+
+
+def fused_rmsnorm_rope_quantize(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    cos: torch.Tensor,
+    sin: torch.Tensor,
+    eps: float = 1e-6,
+    num_heads: int = None,
+    scale: torch.Tensor = None,
+    *,
+    dtype: torch.dtype = torch.uint8,
+) -> tuple:
+    """RMSNorm + RoPE with the output quantized to 8 bits in the same kernel.
+
+    Returns ``(codes, scale)`` equal, byte for byte, to
+    ``quantize_fp8(fused_rmsnorm_rope(x, weight, cos, sin, eps, num_heads), scale, dtype=dtype)``.
+    With ``scale=None`` the dynamic per-tensor scale is derived from maxima the
+    RMSNorm+RoPE pass records while it writes the rows (on shapes where it
+    runs its warp-per-row kernel), so the encode pass needs no separate amax
+    read of the rows. This is the fusion the reference's roadmap pairs with
+    ``FP8Linear`` (a ``FusedRMSNormRoPE`` -> ``FP8Linear`` chain); the
+    reference itself has no such op.
+
+    Args:
+        x, weight, cos, sin, eps, num_heads: as for :func:`fused_rmsnorm_rope`
+        scale: optional quantize multiplier (tensor); None = dynamic per-tensor scale
+        dtype: ``torch.uint8`` (the reference's code) or ``torch.float8_e4m3fn``
+    """
+    from triton_ops.exceptions import UnsupportedDtypeError
+    from triton_ops.kernels.fp8_quantize import _CODE_DTYPES, _scale_f32
+
+    batch_size, seq_len, hidden_dim, head_dim, num_heads = validate_rmsnorm_rope_inputs(x, weight, cos, sin, num_heads)
+    check_rmsnorm_rope_kernel_bounds(x, cos, sin, seq_len, hidden_dim, head_dim, num_heads)
+    if dtype not in _CODE_DTYPES:
+        raise UnsupportedDtypeError(f"codes dtype must be one of {_CODE_DTYPES}, got {dtype}", dtype=dtype,
+                                    supported_dtypes=list(_CODE_DTYPES))
+    if weight.device != x.device:
+        from triton_ops.exceptions import DeviceError
+
+        raise DeviceError("weight must be on x's device", expected_device=str(x.device),
+                          actual_device=str(weight.device), tensor_name="weight")
+    if cos.dim() == 4:
+        cos = cos.squeeze(0).squeeze(1)
+        sin = sin.squeeze(0).squeeze(1)
+    if sin.stride() != cos.stride():
+        cos = cos.contiguous()
+        sin = sin.contiguous()
+    dev = x.device
+    codes = torch.empty(x.shape, dtype=dtype, device=dev)
+    x_code = _lib.dtype_code(x.dtype, "x")
+    s32 = None
+    scale_out = None
+    if scale is None:
+        scale = scale_out = torch.empty((), dtype=torch.float32, device=dev)
+    else:
+        s32 = _scale_f32(scale.to(dev))
+    lib = _lib.load()
+    ws_bytes = lib.tfo_rmsnorm_rope_quantize_workspace_bytes(batch_size, seq_len, hidden_dim, x_code)
+    ws = _lib.workspace(ws_bytes, dev)
+    _lib.call(
+        "tfo_rmsnorm_rope_quantize",
+        x.data_ptr(), weight.data_ptr(), cos.data_ptr(), sin.data_ptr(), codes.data_ptr(),
+        batch_size, seq_len, hidden_dim, head_dim, num_heads, cos.stride(0), cos.stride(1), float(eps),
+        x_code, _lib.dtype_code(weight.dtype, "weight"), _lib.dtype_code(cos.dtype, "cos"),
+        _lib.dtype_code(sin.dtype, "sin"), _lib.ptr(s32), _lib.ptr(scale_out), _lib.dtype_code(dtype),
+        ws.data_ptr(), ws.numel(), _lib.stream_of(x),
+    )
+    return codes, scale
 
 
 def rmsnorm_reference(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
