@@ -722,6 +722,17 @@ def run_profile_op(args):
         qa, sa = triton_ops.quantize_fp8(torch.randn(m, H, device=dev, generator=g).half(), dtype=qd)
         qb, sb = triton_ops.quantize_fp8(torch.randn(H, H, device=dev, generator=g).half(), dtype=qd)
         fn = lambda: triton_ops.fp8_gemm(qa, qb, sa, sb)
+    elif op in ("rmsnorm_rope_quantize", "rmsnorm_rope_quantize_given", "rmsnorm_rope_then_quantize_given"):
+        x = torch.randn(8, S, H, device=dev, generator=g).half()
+        w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).half()
+        cos, sin = rope_tables(S, D, dev)
+        two = torch.tensor(2.0, device=dev)
+        if op == "rmsnorm_rope_quantize":
+            fn = lambda: triton_ops.fused_rmsnorm_rope_quantize(x, w, cos, sin)
+        elif op == "rmsnorm_rope_quantize_given":
+            fn = lambda: triton_ops.fused_rmsnorm_rope_quantize(x, w, cos, sin, scale=two)
+        else:
+            fn = lambda: triton_ops.quantize_fp8(triton_ops.fused_rmsnorm_rope(x, w, cos, sin), two)
     elif op in ("quantize", "dequantize"):
         # [4096, 4096] fp16 N(0, 1) with 0.1% of entries set to +-200
         t = torch.randn(4096, 4096, device=dev, generator=g).half()
