@@ -180,6 +180,18 @@ TFO_API int tfo_fp8_gemm(const void* a, const void* b, const float* a_scale, con
                          int64_t N, int64_t K, int ab_dtype, int b_layout, int out_dtype, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* FP8Linear's forward GEMM: out[M, N] = round_to(gemm_dtype)(x_codes @ w_codesᵀ
+ * decoded and scaled, as tfo_fp8_gemm with b_layout TFO_B_NK) + bias[N], the sum
+ * in fp32 and stored as out_dtype: exactly the reference's
+ * `fp8_gemm(..., output_dtype=x.dtype)` followed by `output + self.bias`
+ * (triton_ops/kernels/fp8_gemm.py:293-309), with the bias added in the GEMM's
+ * epilogue instead of a separate pass. bias == NULL: tfo_fp8_gemm with
+ * out_dtype = gemm_dtype. Workspace: tfo_fp8_gemm_workspace_bytes(M, N, K,
+ * ab_dtype, TFO_B_NK). No separate counterpart in the reference. */
+TFO_API int tfo_fp8_linear(const void* x_codes, const void* w_codes, const float* x_scale, const float* w_scale,
+                           const void* bias, int bias_dtype, void* out, int64_t M, int64_t N, int64_t K, int ab_dtype,
+                           int gemm_dtype, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
+
 /* Workspace bytes tfo_gated_mlp needs (non-zero only when an fp32 copy of an
  * operand is required, i.e. mixed or fp32 dtypes). */
 TFO_API size_t tfo_gated_mlp_workspace_bytes(int64_t M, int64_t N, int64_t K, int x_dtype, int w_dtype);

@@ -237,3 +237,26 @@ def test_pair_and_single_cta_tiles_agree(cuda, tmp_path):
     single = np.load(tmp_path / "single.npy")
     pair = fp8_gemm(qa, qb, sa, sb, torch.float16).cpu().numpy()
     np.testing.assert_array_equal(pair.view(np.uint16), single.view(np.uint16))
+
+
+@pytest.mark.parametrize("M", [16, 256, 1000])
+@pytest.mark.parametrize("xdt,bdt", [(torch.float16, torch.float32), (torch.bfloat16, torch.float32),
+                                     (torch.float32, torch.float32), (torch.float16, torch.float16)])
+def test_fp8linear_bias_in_epilogue(cuda, M, xdt, bdt):
+    """FP8Linear's bias, added in the GEMM epilogue, equals fp8_gemm(...) + bias bit for bit (dtype promotion too)."""
+    from triton_ops import FP8Linear
+    from triton_ops import _lib
+    from triton_ops.kernels.fp8_gemm import _gemm_codes
+    from triton_ops.kernels.fp8_quantize import quantize_fp8
+
+    g = torch.Generator(device="cuda").manual_seed(M)
+    lin = FP8Linear(512, 4096, bias=True).cuda()
+    with torch.no_grad():
+        lin.bias.copy_(torch.randn(4096, device="cuda", generator=g))
+    lin.bias.data = lin.bias.data.to(bdt)
+    x = torch.randn(M, 512, device="cuda", generator=g).to(xdt)
+    y = lin(x)
+    xq, xs = quantize_fp8(x)
+    ref = _gemm_codes(xq, lin.weight_fp8, xs, lin.weight_scale, xdt, _lib.B_NK) + lin.bias
+    assert y.dtype == ref.dtype and y.shape == ref.shape
+    assert torch.equal(y, ref)

@@ -397,6 +397,33 @@ int tfo_fp8_gemm(const void* a, const void* b, const float* a_scale, const float
   return TFO_OK;
 }
 
+int tfo_fp8_linear(const void* x_codes, const void* w_codes, const float* x_scale, const float* w_scale,
+                   const void* bias, int bias_dtype, void* out, int64_t M, int64_t N, int64_t K, int ab_dtype,
+                   int gemm_dtype, int out_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* fn = "tfo_fp8_linear";
+  if (bias == nullptr)
+    return tfo_fp8_gemm(x_codes, w_codes, x_scale, w_scale, out, M, N, K, ab_dtype, TFO_B_NK, gemm_dtype, workspace,
+                        workspace_bytes, stream);
+  if (ab_dtype != U8 && ab_dtype != E4M3) return fail(TFO_ERR_DTYPE, std::string(fn) + ": operands must be U8 or E4M3");
+  if (!is_float_dtype(gemm_dtype) || !is_float_dtype(out_dtype) || !is_float_dtype(bias_dtype))
+    return fail(TFO_ERR_DTYPE, std::string(fn) + ": gemm, bias and output dtypes must be f16, bf16 or f32");
+  if (M < 0 || N < 0 || K <= 0) return fail(TFO_ERR_INVALID, std::string(fn) + ": bad dimension (K must be positive)");
+  if (M > INT32_MAX || N > INT32_MAX || K > 131072)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": M, N must fit in int32 and K <= 131072");
+  if (M == 0 || N == 0) return TFO_OK;
+  if (!x_codes || !w_codes || !x_scale || !w_scale || !out) return fail(TFO_ERR_INVALID, std::string(fn) + ": NULL pointer");
+  Fp8GemmArgs g{x_codes, w_codes, x_scale, w_scale, out, M, N, K, ab_dtype, TFO_B_NK, out_dtype, workspace,
+                workspace_bytes};
+  g.bias = bias;
+  g.bias_dtype = bias_dtype;
+  g.round_dtype = gemm_dtype;
+  if (workspace_bytes < fp8_gemm_workspace_bytes(g) || !workspace)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": workspace smaller than tfo_fp8_gemm_workspace_bytes()");
+  const cudaError_t e = fp8_gemm_launch(g, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return TFO_OK;
+}
+
 size_t tfo_gated_mlp_workspace_bytes(int64_t M, int64_t N, int64_t K, int x_dtype, int w_dtype) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   GatedMlpArgs g{};

@@ -128,6 +128,11 @@ struct Fp8GemmArgs {
   int ab_dtype, b_layout, out_dtype;
   void* ws;
   size_t ws_bytes;
+  // FP8Linear: bias[N] added after rounding the product to round_dtype
+  // (< 0: no rounding step), result stored as out_dtype
+  const void* bias = nullptr;
+  int bias_dtype = -1;
+  int round_dtype = -1;
 };
 size_t fp8_gemm_workspace_bytes(const Fp8GemmArgs& g);
 // Launch choice of tfo_fp8_gemm for 16-byte-aligned operands: out = {rows

@@ -182,6 +182,20 @@ __global__ void __launch_bounds__(kColThreads) prep_cols_s8_sum_kernel(const uin
 // (raw u8 = int8 value + 128); then acc = exact + 128 * (sum of the other
 // operand's int8 values along K), which corr_row (per output row, the A sums)
 // or corr_col (per output column, the B sums) removes.
+// FP8Linear's `fp8_gemm(...) + bias`: the product rounded to the GEMM's
+// output dtype, then the bias added in fp32 (torch's arithmetic for the sum).
+__device__ __forceinline__ float round_to_dtype(float v, int dt) {
+  if (dt == F16) return __half2float(__float2half_rn(v));
+  if (dt == BF16) return __bfloat162float(__float2bfloat16_rn(v));
+  return v;
+}
+__device__ __forceinline__ void linear_bias16(float (&v)[16], const void* bias, int bias_dt, int round_dt, int col0,
+                                              int valid) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (i < valid) v[i] = __fadd_rn(round_to_dtype(v[i], round_dt), load_as_float(bias, col0 + i, bias_dt));
+}
+
 template <typename TO, bool INT_ACC>
 struct Fp8Epi {
   struct Params {
@@ -194,6 +208,8 @@ struct Fp8Epi {
     const int32_t* corr_row;
     const int32_t* corr_col;
     uint32_t* partial;  // split-K: [splits][M][N] raw accumulators
+    const void* bias;   // FP8Linear: bias[N] of dtype bias_dt, added after rounding to round_dt
+    int bias_dt, round_dt;
   };
   // alpha = fp32(codec_k / (sa * sb)), computed once per thread
   struct State {
@@ -254,6 +270,7 @@ struct Fp8Epi {
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[0][i]) * alpha;
     }
+    if (p.bias != nullptr) linear_bias16(v, p.bias, p.bias_dt, p.round_dt, col0, valid);
     store_row16<TO>(p.out + static_cast<int64_t>(row) * p.ldc + col0, v, valid, p.vec_ok);
   }
 };
@@ -266,7 +283,8 @@ __global__ void __launch_bounds__(256) fp8_splitk_finalize_kernel(const uint32_t
                                                                   const float* __restrict__ sb, double codec_k,
                                                                   const int32_t* __restrict__ corr_row,
                                                                   const int32_t* __restrict__ corr_col,
-                                                                  TO* __restrict__ out) {
+                                                                  const void* __restrict__ bias, int bias_dt,
+                                                                  int round_dt, TO* __restrict__ out) {
   const float alpha = static_cast<float>(codec_k / (static_cast<double>(__ldg(sa)) * __ldg(sb)));
   const int64_t total = M * N;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -283,7 +301,9 @@ __global__ void __launch_bounds__(256) fp8_splitk_finalize_kernel(const uint32_t
       for (int s = 0; s < splits; ++s) acc += __uint_as_float(partial[s * total + i]);
       v = acc;
     }
-    out[i] = Ty<TO>::from_f(v * alpha);
+    float r = v * alpha;
+    if (bias != nullptr) r = __fadd_rn(round_to_dtype(r, round_dt), load_as_float(bias, i % N, bias_dt));
+    out[i] = Ty<TO>::from_f(r);
   }
 }
 
@@ -384,7 +404,7 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
   const double codec_k = INT_ACC ? (448.0 / 127.0) * (448.0 / 127.0) : 1.0;
   typename Epi::Params ep{static_cast<TO*>(g.c), g.sa, g.sb, codec_k, g.N,
                           al16(g.c) && (g.N * sizeof(TO)) % 16 == 0, corr_row, corr_col,
-                          p.splits > 1 ? partial : nullptr};
+                          p.splits > 1 ? partial : nullptr, g.bias, g.bias_dtype, g.round_dtype};
   const int64_t work = ((g.M + L::PAIR_M - 1) / L::PAIR_M) * ((g.N + BN - 1) / BN) * p.splits;
   if constexpr (CG == 1 && BN == 128) {
     if (p.ksplit_cluster) {
@@ -411,7 +431,8 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
   const int64_t total = g.M * g.N;
   const int fgrid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, num_sms() * 8)));
   fp8_splitk_finalize_kernel<TO, INT_ACC><<<fgrid, 256, 0, st>>>(partial, p.splits, g.M, g.N, g.sa, g.sb, codec_k,
-                                                                 corr_row, corr_col, static_cast<TO*>(g.c));
+                                                                 corr_row, corr_col, g.bias, g.bias_dtype,
+                                                                 g.round_dtype, static_cast<TO*>(g.c));
   note_launch();
   return cudaGetLastError();
 }

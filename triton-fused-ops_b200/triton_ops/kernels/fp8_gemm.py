@@ -9,7 +9,8 @@ reference (triton_ops/kernels/fp8_gemm.py:123-187).
 
 ``FP8Linear`` keeps the reference's parameters and buffers
 (fp8_gemm.py:228-310) but hands the [out, in] code matrix to the GEMM as is
-(no per-call transpose).
+(no per-call transpose) and adds the bias in the GEMM's epilogue
+(``tfo_fp8_linear``), with the reference's rounding and dtype promotion.
 
 ``fp8_gemm_reference`` restates the reference's PyTorch oracle (:190-225) for
 tests; the op never calls it.
@@ -60,6 +61,30 @@ def _gemm_codes(a, b, a_scale, b_scale, output_dtype, b_layout):
         b_layout, _lib.dtype_code(output_dtype, "output_dtype"), ws.data_ptr(), ws.numel(), _lib.stream_of(a),
     )
     return c
+
+
+def _linear_bias(x_codes, w_codes, x_scale, w_scale, bias, gemm_dtype):
+    """`fp8_gemm(x, w.t(), output_dtype=gemm_dtype) + bias` with the bias added in the GEMM epilogue.
+
+    The result has torch's promoted dtype of the two operands of the sum, and the
+    same values: the product rounded to `gemm_dtype`, plus the bias in fp32.
+    """
+    M, K = x_codes.shape
+    N = w_codes.shape[0]
+    res_dtype = torch.promote_types(gemm_dtype, bias.dtype)
+    out = torch.empty(M, N, dtype=res_dtype, device=x_codes.device)
+    if out.numel() == 0:
+        return out
+    b = bias.to(x_codes.device).contiguous()
+    code = _lib.dtype_code(x_codes.dtype, "x")
+    ws = _lib.workspace(_lib.load().tfo_fp8_gemm_workspace_bytes(M, N, K, code, _lib.B_NK), x_codes.device)
+    _lib.call(
+        "tfo_fp8_linear", x_codes.data_ptr(), w_codes.data_ptr(), _scale_f32(x_scale.to(x_codes.device)).data_ptr(),
+        _scale_f32(w_scale.to(x_codes.device)).data_ptr(), b.data_ptr(), _lib.dtype_code(b.dtype, "bias"),
+        out.data_ptr(), M, N, K, code, _lib.dtype_code(gemm_dtype), _lib.dtype_code(res_dtype), ws.data_ptr(),
+        ws.numel(), _lib.stream_of(x_codes),
+    )
+    return out
 
 
 def fp8_gemm(
@@ -148,8 +173,8 @@ class FP8Linear(torch.nn.Module):
         x_fp8, x_scale = quantize_fp8(x_2d)
         out_dtype = x.dtype if x.dtype in SUPPORTED_DTYPES_FLOAT else torch.float16
         # weight_fp8 is [out, in] = [N, K]: consumed directly as the K-major B operand.
-        output = _gemm_codes(x_fp8, self.weight_fp8, x_scale, self.weight_scale, out_dtype, _lib.B_NK)
-        output = output.view(*orig_shape[:-1], self.out_features)
-        if self.bias is not None:
-            output = output + self.bias
-        return output
+        if self.bias is None:
+            output = _gemm_codes(x_fp8, self.weight_fp8, x_scale, self.weight_scale, out_dtype, _lib.B_NK)
+        else:
+            output = _linear_bias(x_fp8, self.weight_fp8, x_scale, self.weight_scale, self.bias, out_dtype)
+        return output.view(*orig_shape[:-1], self.out_features)
