@@ -451,6 +451,17 @@ def components(peaks, flush_buf):
         us, err = time_graph([lambda x=x: triton_ops.fused_gated_mlp(x, wg, wu, act) for x in xm], reps=10)
         us_call = 1e3 * time_events(lambda: triton_ops.fused_gated_mlp(xm[0], wg, wu, act), 20, flush_buf)
         out[f"gated_mlp_2x1024x4096_{act}"] = entry(us, err, us_call, flops=fl, peak=peaks["bf16_tflops"])
+    # the same MLP with 8-bit output codes (given / dynamic scale) against the two ops
+    sc = torch.tensor(40.0, device=dev)
+    mq = {}
+    us, err = time_graph([lambda x=x: triton_ops.fused_gated_mlp_quantize(x, wg, wu, "silu", sc) for x in xm], reps=10)
+    mq["given_scale"] = entry(us, err, None, flops=fl, peak=peaks["bf16_tflops"])
+    us, err = time_graph([lambda x=x: triton_ops.fused_gated_mlp_quantize(x, wg, wu, "silu") for x in xm], reps=10)
+    mq["dynamic_scale"] = entry(us, err, None, flops=fl, peak=peaks["bf16_tflops"])
+    us, err = time_graph([lambda x=x: triton_ops.quantize_fp8(triton_ops.fused_gated_mlp(x, wg, wu, "silu"), sc)
+                          for x in xm], reps=10)
+    mq["unfused_given_scale"] = entry(us, err, None, flops=fl, peak=peaks["bf16_tflops"])
+    out["gated_mlp_quantize_2x1024x4096_silu"] = mq
     return out
 
 

@@ -204,6 +204,24 @@ TFO_API int tfo_gated_mlp(const void* x, const void* w_gate, const void* w_up, v
                           int64_t K, int x_dtype, int w_dtype, int activation, void* workspace,
                           size_t workspace_bytes, void* stream);
 
+/* The gated MLP with its output as 8-bit codes (code_dtype TFO_DTYPE_U8: the
+ * reference codec; TFO_DTYPE_E4M3) for an FP8 down-projection: codes and scale
+ * equal tfo_fp8_quantize of the tfo_gated_mlp output byte for byte. Given
+ * scale on the tcgen05 path: the epilogue rounds each output to x's dtype
+ * and writes its code directly (no output rows in memory, no encode pass).
+ * scale == NULL: the epilogue writes the rows to the workspace and one max
+ * per epilogue warp, and the encode pass derives the scale from those (no
+ * separate amax read). CUDA-core shapes run the two ops. Workspace:
+ * tfo_gated_mlp_quantize_workspace_bytes with the same pointers and
+ * has_scale = (scale != NULL). No counterpart in the reference: the MLP ->
+ * FP8 down-projection chain of its roadmap. */
+TFO_API size_t tfo_gated_mlp_quantize_workspace_bytes(const void* x, const void* w_gate, const void* w_up, int64_t M,
+                                                      int64_t N, int64_t K, int x_dtype, int w_dtype, int has_scale);
+TFO_API int tfo_gated_mlp_quantize(const void* x, const void* w_gate, const void* w_up, void* codes, int64_t M,
+                                   int64_t N, int64_t K, int x_dtype, int w_dtype, int activation, const float* scale,
+                                   float* scale_out, int code_dtype, void* workspace, size_t workspace_bytes,
+                                   void* stream);
+
 #ifdef __cplusplus
 }
 #endif

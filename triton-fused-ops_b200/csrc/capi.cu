@@ -463,6 +463,96 @@ int tfo_gated_mlp(const void* x, const void* w_gate, const void* w_up, void* out
   return TFO_OK;
 }
 
+namespace {
+inline size_t round256(size_t v) { return (v + 255) / 256 * 256; }
+// Workspace layout of tfo_gated_mlp_quantize: [MLP workspace][rows][partials / quantize workspace]
+struct MlpQuantLayout {
+  size_t mlp, rows, tail, total;
+  bool tensor, one_pass;
+};
+MlpQuantLayout mlp_quant_layout(const void* x, const void* wg, const void* wu, int64_t M, int64_t N, int64_t K,
+                                int x_dtype, int w_dtype, bool has_scale) {
+  GatedMlpArgs g{x, wg, wu, nullptr, M, N, K, x_dtype, w_dtype, 0, nullptr, 0};
+  MlpQuantLayout l{};
+  l.mlp = round256(gated_mlp_workspace_bytes(g));
+  l.tensor = gated_mlp_tensor_path(g);
+  l.one_pass = has_scale && l.tensor;
+  const int64_t n = M * N;
+  l.rows = l.one_pass ? 0 : round256(static_cast<size_t>(n) * (x_dtype == F32 ? 4 : 2));
+  l.tail = std::max(sizeof(uint32_t) * 4 * static_cast<size_t>(gated_mlp_max_ctas()), scale_workspace_bytes(n));
+  l.total = l.mlp + l.rows + l.tail;
+  return l;
+}
+}  // namespace
+
+size_t tfo_gated_mlp_quantize_workspace_bytes(const void* x, const void* w_gate, const void* w_up, int64_t M,
+                                              int64_t N, int64_t K, int x_dtype, int w_dtype, int has_scale) {
+  if (M <= 0 || N <= 0 || K <= 0) return 16;
+  return mlp_quant_layout(x, w_gate, w_up, M, N, K, x_dtype, w_dtype, has_scale != 0).total;
+}
+
+int tfo_gated_mlp_quantize(const void* x, const void* w_gate, const void* w_up, void* codes, int64_t M, int64_t N,
+                           int64_t K, int x_dtype, int w_dtype, int activation, const float* scale, float* scale_out,
+                           int code_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* fn = "tfo_gated_mlp_quantize";
+  if (!is_float_dtype(x_dtype) || !is_float_dtype(w_dtype))
+    return fail(TFO_ERR_DTYPE, std::string(fn) + ": dtypes must be f16, bf16 or f32");
+  if (code_dtype != U8 && code_dtype != E4M3) return fail(TFO_ERR_DTYPE, std::string(fn) + ": codes must be U8 or E4M3");
+  if (activation < TFO_ACT_SILU || activation > TFO_ACT_GELU_TANH)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": unknown activation");
+  if (M < 0 || N < 0 || K <= 0) return fail(TFO_ERR_INVALID, std::string(fn) + ": bad dimension (K must be positive)");
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": dimensions must fit in int32");
+  if (scale == nullptr && scale_out == nullptr)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": a dynamic scale needs scale_out");
+  auto st = static_cast<cudaStream_t>(stream);
+  if (M == 0 || N == 0) {
+    if (scale != nullptr) return TFO_OK;
+    if (!workspace || workspace_bytes < sizeof(uint32_t))
+      return fail(TFO_ERR_INVALID, std::string(fn) + ": workspace too small");
+    uint32_t* parts = static_cast<uint32_t*>(workspace);
+    cudaError_t e = amax_partials_launch(x, 0, x_dtype, parts, 1, st);
+    if (e == cudaSuccess) e = finalize_scale_launch(parts, 1, scale_out, st);
+    return e == cudaSuccess ? TFO_OK : cuda_fail(e, fn);
+  }
+  if (!x || !w_gate || !w_up || !codes) return fail(TFO_ERR_INVALID, std::string(fn) + ": NULL pointer");
+  const MlpQuantLayout l = mlp_quant_layout(x, w_gate, w_up, M, N, K, x_dtype, w_dtype, scale != nullptr);
+  if (!workspace || workspace_bytes < l.total)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": workspace smaller than tfo_gated_mlp_quantize_workspace_bytes()");
+  char* ws = static_cast<char*>(workspace);
+  void* rows = ws + l.mlp;
+  void* tail = ws + l.mlp + l.rows;
+  const int64_t n = M * N;
+  GatedMlpArgs g{x, w_gate, w_up, nullptr, M, N, K, x_dtype, w_dtype, activation, ws, l.mlp};
+  cudaError_t e;
+  if (l.one_pass) {
+    // codes straight from the MLP epilogue
+    g.codes = static_cast<uint8_t*>(codes);
+    g.scale = scale;
+    g.e4m3 = code_dtype == E4M3 ? 1 : 0;
+    e = gated_mlp_launch(g, st);
+  } else if (l.tensor) {
+    // rows + one max per epilogue warp, then the encode reduces the maxima to the scale
+    int ctas = 0;
+    g.out = rows;
+    g.amax_parts = static_cast<uint32_t*>(tail);
+    g.ctas_out = &ctas;
+    e = gated_mlp_launch(g, st);
+    if (e == cudaSuccess)
+      e = encode_launch(rows, n, x_dtype, nullptr, static_cast<uint32_t*>(tail), 4 * ctas, scale_out, codes,
+                        code_dtype, st);
+  } else {
+    // CUDA-core MLP: the rows, then the ordinary quantize
+    g.out = rows;
+    e = gated_mlp_launch(g, st);
+    if (e == cudaSuccess)
+      e = scale != nullptr ? encode_launch(rows, n, x_dtype, scale, nullptr, 0, nullptr, codes, code_dtype, st)
+                           : quantize_dynamic_launch(rows, n, x_dtype, scale_out, codes, code_dtype, tail, l.tail, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return TFO_OK;
+}
+
 int tfo_selftest_bounded_wait(int64_t budget_cycles, void* stream) {
   if (budget_cycles <= 0 || budget_cycles > (1ll << 32))
     return fail(TFO_ERR_INVALID, "tfo_selftest_bounded_wait: budget must be in (0, 2^32] cycles");

@@ -152,7 +152,20 @@ struct GatedMlpArgs {
   int x_dtype, w_dtype, act;
   void* ws;
   size_t ws_bytes;
+  // 8-bit output (tfo_gated_mlp_quantize): codes of the outputs rounded to x's
+  // dtype with the given scale (out may then be NULL), and/or one max |output|
+  // per epilogue warp (4 per CTA) to amax_parts
+  uint8_t* codes = nullptr;
+  const float* scale = nullptr;
+  int e4m3 = 0;
+  uint32_t* amax_parts = nullptr;
+  int* ctas_out = nullptr;  // receives the tcgen05 kernel's CTA count (4 amax partials each)
 };
 size_t gated_mlp_workspace_bytes(const GatedMlpArgs& g);
 cudaError_t gated_mlp_launch(const GatedMlpArgs& g, cudaStream_t st);
+// True when gated_mlp_launch runs the tcgen05 kernel (which supports the 8-bit
+// output); otherwise it runs the CUDA-core kernel.
+bool gated_mlp_tensor_path(const GatedMlpArgs& g);
+// Upper bound on the CTAs of the tcgen05 kernel (amax partials: 4 per CTA).
+int gated_mlp_max_ctas();
 }  // namespace tfo

@@ -229,7 +229,8 @@ struct Fp8Epi {
     q.partial = nullptr;
     return q;
   }
-  __device__ __forceinline__ void operator()(const Params& p, const State& st, const uint32_t (&r)[1][16], int row,
+  static __device__ __forceinline__ void finish(const Params&, State&) {}
+  __device__ __forceinline__ void operator()(const Params& p, State& st, const uint32_t (&r)[1][16], int row,
                                              int col0, int M, int N, int split) const {
     if (row >= M || col0 >= N) return;
     const int valid = min(16, N - col0);

@@ -17,6 +17,7 @@
 // Shapes TMA cannot address (row pitch not a multiple of 16 bytes) use a
 // CUDA-core tiled kernel.
 #include "capi_internal.h"
+#include "codec.cuh"
 #include "common.cuh"
 #include "epilogue.cuh"
 #include "gemm_sm100.cuh"
@@ -51,16 +52,63 @@ struct GatedEpi {
     TO* out;
     int64_t ldc;
     bool vec_ok;
+    uint8_t* codes;         // optional 8-bit output
+    const float* scale;     // its multiplier
+    int e4m3;               // codes are e4m3 (else the reference codec)
+    uint32_t* amax_parts;   // optional: one max |output| per epilogue warp
   };
-  struct State {};
-  static __device__ __forceinline__ State init(const Params&) { return {}; }
-  __device__ __forceinline__ void operator()(const Params& p, const State&, const uint32_t (&r)[2][16], int row,
+  struct State {
+    float s;        // code multiplier
+    uint32_t amax;  // running max of |output| (fp32 bits of the TO-rounded values)
+  };
+  static __device__ __forceinline__ State init(const Params& p) {
+    return {p.codes != nullptr ? *p.scale : 0.f, 0u};
+  }
+  static __device__ __forceinline__ void finish(const Params& p, State& st) {
+    if (p.amax_parts == nullptr) return;
+    const uint32_t m = warp_max_u32(st.amax);
+    if ((threadIdx.x & 31) == 0) p.amax_parts[blockIdx.x * 4 + ((threadIdx.x >> 5) & 3)] = m;
+  }
+  __device__ __forceinline__ void operator()(const Params& p, State& st, const uint32_t (&r)[2][16], int row,
                                              int col0, int M, int N, int /*split*/) const {
     if (row >= M || col0 >= N) return;
+    const int valid = min(16, N - col0);
     float v[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[0][i]) * act_fn<ACT>(__uint_as_float(r[1][i]));
-    store_row16<TO>(p.out + static_cast<int64_t>(row) * p.ldc + col0, v, min(16, N - col0), p.vec_ok);
+    if (p.out != nullptr) store_row16<TO>(p.out + static_cast<int64_t>(row) * p.ldc + col0, v, valid, p.vec_ok);
+    if (p.codes == nullptr && p.amax_parts == nullptr) return;
+    // the values the TO output holds
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = Ty<TO>::to_f(Ty<TO>::from_f(v[i]));
+    if (p.amax_parts != nullptr) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i < valid) st.amax = max(st.amax, __float_as_uint(fabsf(v[i])));
+    }
+    if (p.codes != nullptr) {
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float c = __fmul_rn(v[4 * q + j], st.s);
+          const uint32_t b = p.e4m3 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(c, __NV_SATFINITE, __NV_E4M3))
+                                    : ref_encode(c);
+          word |= b << (8 * j);
+        }
+        w[q] = word;
+      }
+      uint8_t* dst = p.codes + static_cast<int64_t>(row) * p.ldc + col0;
+      if (valid == 16 && (reinterpret_cast<uintptr_t>(dst) & 15u) == 0) {
+        *reinterpret_cast<uint4*>(dst) = make_uint4(w[0], w[1], w[2], w[3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (i < valid) dst[i] = static_cast<uint8_t>(w[i >> 2] >> (8 * (i & 3)));
+      }
+    }
   }
 };
 
@@ -152,9 +200,11 @@ cudaError_t launch_umma_cg(const CUtensorMap& tx, const CUtensorMap& tg, const C
   auto kern = umma_gemm_kernel<KIND, kBlockN, 2, STAGES, Epi, false, CG>;
   const int resident = gemm_resident_units(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, CG);
   if (resident <= 0) return cudaErrorInvalidConfiguration;
-  typename Epi::Params ep{static_cast<TO*>(g.out), g.N, al16(g.out) && (g.N * sizeof(TO)) % 16 == 0};
+  typename Epi::Params ep{static_cast<TO*>(g.out), g.N, al16(g.out) && (g.N * sizeof(TO)) % 16 == 0, g.codes,
+                          g.scale, g.e4m3, g.amax_parts};
   const int64_t tiles = ((g.M + L::PAIR_M - 1) / L::PAIR_M) * ((g.N + kBlockN - 1) / kBlockN);
   const int units = static_cast<int>(std::min<int64_t>(tiles, resident));
+  if (g.ctas_out != nullptr) *g.ctas_out = units * CG;
   cudaError_t e = launch_gemm_units(kern, CG, units, L::SMEM_BYTES, st, tx, tg, tu, static_cast<int>(g.M),
                                     static_cast<int>(g.N), static_cast<int>(g.K), kGroupM, idesc, ep,
                                     error_word_ptr(), 1);
@@ -234,6 +284,10 @@ void gated_mlp_tile(int64_t M, int64_t N, int64_t K, int32_t out[6]) {
   out[4] = 1;
   out[5] = kGroupM;
 }
+
+bool gated_mlp_tensor_path(const GatedMlpArgs& g) { return plan_mlp(g).path != Path::SIMT; }
+
+int gated_mlp_max_ctas() { return 2 * num_sms(); }
 
 cudaError_t gated_mlp_launch(const GatedMlpArgs& g, cudaStream_t st) {
   const MlpPlan p = plan_mlp(g);

@@ -109,11 +109,13 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 
 // Epi must provide:
 //   struct Params;
-//   struct State;  values each epilogue thread derives once from Params
+//   struct State;  per epilogue thread: values derived once from Params, running values
 //   static __device__ State init(const Params&);
-//   __device__ void operator()(const Params&, const State&, const uint32_t (&acc)[NUM_B][16], int row, int col0,
+//   __device__ void operator()(const Params&, State&, const uint32_t (&acc)[NUM_B][16], int row, int col0,
 //                              int M, int N, int split)
-//   called once per 16 accumulator columns per row (row < M not guaranteed).
+//   called once per 16 accumulator columns per row (row < M not guaranteed);
+//   static __device__ void finish(const Params&, State&)
+//   called by every epilogue thread (4 full warps) after its last tile.
 //
 // B_MN: the B operand is MN-major (B given as [K, N] with N contiguous, as
 // the reference's fp8_gemm passes it); each stage then holds B_ROWS / 128
@@ -317,7 +319,7 @@ __global__ void __launch_bounds__(192, 1)
     const int sub = warp & 3;
     const int row_in_tile = static_cast<int>(rank) * L::BM + sub * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
-    const typename Epi::State est = Epi::init(ep);
+    typename Epi::State est = Epi::init(ep);
     int tcount = 0;
     for (int w = unit; w < num_work; w += num_units, ++tcount) {
       const int acc = tcount & 1;
@@ -372,13 +374,14 @@ __global__ void __launch_bounds__(192, 1)
         else mbar_arrive(&tempty[acc]);
       }
     }
+    Epi::finish(ep, est);
   }
 
   __syncthreads();
   if constexpr (KSPLIT) {
     cluster_sync();  // every slice's tile is in shared memory
     if (warp >= 2) {
-      const typename Epi::State est = Epi::init(ep);
+      typename Epi::State est = Epi::init(ep);
       const typename Epi::Params epf = Epi::final_params(ep);
       const Work wk = work(blockIdx.x);
       const int rows_per = (L::BM + k_splits - 1) / k_splits;

@@ -39,7 +39,7 @@ from triton_ops.exceptions import (
 )
 from triton_ops.kernels.fp8_gemm import FP8Linear, fp8_gemm
 from triton_ops.kernels.fp8_quantize import dequantize_fp8, quantize_fp8
-from triton_ops.kernels.gated_mlp import FusedGatedMLP, fused_gated_mlp
+from triton_ops.kernels.gated_mlp import FusedGatedMLP, fused_gated_mlp, fused_gated_mlp_quantize
 from triton_ops.kernels.rmsnorm_rope import FusedRMSNormRoPE, fused_rmsnorm_rope, fused_rmsnorm_rope_quantize
 from triton_ops.models import (
     FP8Format,
@@ -56,6 +56,7 @@ __all__ = [
     "fused_rmsnorm_rope_quantize",
     "FusedRMSNormRoPE",
     "fused_gated_mlp",
+    "fused_gated_mlp_quantize",
     "FusedGatedMLP",
     "fp8_gemm",
     "FP8Linear",

@@ -79,6 +79,13 @@ _SIGNATURES = {
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_vp,
          _c_size, _c_vp],
     ),
+    "tfo_gated_mlp_quantize_workspace_bytes": (_c_size, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
+                                                          _c_int]),
+    "tfo_gated_mlp_quantize": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_vp, _c_vp, _c_int, _c_vp,
+         _c_size, _c_vp],
+    ),
     "tfo_gated_mlp_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64, _c_int, _c_int]),
     "tfo_gated_mlp": (
         _c_int,

@@ -22,6 +22,9 @@ from triton_ops.validation import validate_gated_mlp_inputs
 fused_gated_mlp_kernel = NativeKernel(
     "fused_gated_mlp_kernel", "tfo_gated_mlp", "shared A tile, two TMEM accumulators, activation in the epilogue"
 )
+fused_gated_mlp_quantize_kernel = NativeKernel(
+    "fused_gated_mlp_quantize_kernel", "tfo_gated_mlp_quantize", "gated MLP with 8-bit codes from the epilogue"
+)
 
 
 def fused_gated_mlp(
@@ -52,6 +55,57 @@ def fused_gated_mlp(
         _lib.stream_of(x),
     )
     return out
+
+
+def fused_gated_mlp_quantize(
+    x: torch.Tensor,
+    gate_weight: torch.Tensor,
+    up_weight: torch.Tensor,
+    activation: str = "silu",
+    scale: torch.Tensor = None,
+    *,
+    dtype: torch.dtype = torch.uint8,
+) -> tuple:
+    """Gated MLP whose output comes back as 8-bit codes, for an FP8 down-projection.
+
+    Returns ``(codes, scale)`` equal, byte for byte, to
+    ``quantize_fp8(fused_gated_mlp(x, gate_weight, up_weight, activation), scale, dtype=dtype)``.
+    With a given `scale` the MLP epilogue writes the codes directly (the
+    [M, intermediate] output never reaches memory); with ``scale=None`` the
+    epilogue also records per-warp maxima of the output, from which the encode
+    pass derives the scale without a separate amax read. The reference has no
+    such op; its roadmap chains the gated MLP into an ``FP8Linear``.
+    """
+    from triton_ops.exceptions import UnsupportedDtypeError
+    from triton_ops.kernels.fp8_quantize import _CODE_DTYPES, _scale_f32
+
+    batch_size, seq_len, hidden_dim, intermediate_dim = validate_gated_mlp_inputs(x, gate_weight, up_weight, activation)
+    if dtype not in _CODE_DTYPES:
+        raise UnsupportedDtypeError(f"codes dtype must be one of {_CODE_DTYPES}, got {dtype}", dtype=dtype,
+                                    supported_dtypes=list(_CODE_DTYPES))
+    dev = x.device
+    if up_weight.dtype != gate_weight.dtype:
+        up_weight = up_weight.to(gate_weight.dtype)
+    codes = torch.empty(batch_size, seq_len, intermediate_dim, dtype=dtype, device=dev)
+    s32 = scale_out = None
+    if scale is None:
+        scale = scale_out = torch.empty((), dtype=torch.float32, device=dev)
+    else:
+        s32 = _scale_f32(scale.to(dev))
+    M = batch_size * seq_len
+    x_code = _lib.dtype_code(x.dtype, "x")
+    w_code = _lib.dtype_code(gate_weight.dtype, "gate_weight")
+    lib = _lib.load()
+    ws_bytes = lib.tfo_gated_mlp_quantize_workspace_bytes(x.data_ptr(), gate_weight.data_ptr(), up_weight.data_ptr(), M,
+                                                          intermediate_dim, hidden_dim, x_code, w_code,
+                                                          int(s32 is not None))
+    ws = _lib.workspace(ws_bytes, dev)
+    _lib.call(
+        "tfo_gated_mlp_quantize", x.data_ptr(), gate_weight.data_ptr(), up_weight.data_ptr(), codes.data_ptr(), M,
+        intermediate_dim, hidden_dim, x_code, w_code, _lib.ACT_CODE[activation], _lib.ptr(s32), _lib.ptr(scale_out),
+        _lib.dtype_code(dtype), ws.data_ptr(), ws.numel(), _lib.stream_of(x),
+    )
+    return codes, scale
 
 
 def gated_mlp_reference(
