@@ -180,6 +180,31 @@ TFO_API int tfo_fp8_gemm(const void* a, const void* b, const float* a_scale, con
                          int64_t N, int64_t K, int ab_dtype, int b_layout, int out_dtype, void* workspace,
                          size_t workspace_bytes, void* stream);
 
+/* Per-token / per-channel scales (extension; the reference's quantize_fp8
+ * reads one scale, its FP8Format.compute_scale_per_channel,
+ * triton_ops/models.py:301-314, computes per-channel ones in torch):
+ * tfo_fp8_compute_scale_rows: scales[r] = 448 / max|x[r, :]| (a zero max
+ *   counts as 1) for a contiguous [rows, cols] x, with torch's rounding of
+ *   compute_scale_per_channel(x, dim=-1) in x's dtype (reciprocal, then
+ *   * 448), stored as fp32;
+ * tfo_fp8_quantize_rows / tfo_fp8_dequantize_rows: the per-tensor codec with
+ *   scales[r] for row r;
+ * tfo_fp8_gemm_scaled: tfo_fp8_gemm with a per-row A scale vector [M]
+ *   (a_per_row = 1, else a_scales[0]) and/or a per-column B scale vector [N]
+ *   (b_per_col = 1), applied in the epilogue; workspace
+ *   tfo_fp8_gemm_scaled_workspace_bytes. */
+TFO_API int tfo_fp8_compute_scale_rows(const void* x, int64_t rows, int64_t cols, int x_dtype, float* scales,
+                                       void* stream);
+TFO_API int tfo_fp8_quantize_rows(const void* x, int64_t rows, int64_t cols, int x_dtype, const float* scales, void* out,
+                                  int out_dtype, void* stream);
+TFO_API int tfo_fp8_dequantize_rows(const void* q, int64_t rows, int64_t cols, int q_dtype, const float* scales,
+                                    void* out, int out_dtype, void* stream);
+TFO_API size_t tfo_fp8_gemm_scaled_workspace_bytes(int64_t M, int64_t N, int64_t K, int ab_dtype, int b_layout);
+TFO_API int tfo_fp8_gemm_scaled(const void* a, const void* b, const float* a_scales, int a_per_row,
+                                const float* b_scales, int b_per_col, void* c, int64_t M, int64_t N, int64_t K,
+                                int ab_dtype, int b_layout, int out_dtype, void* workspace, size_t workspace_bytes,
+                                void* stream);
+
 /* FP8Linear's forward GEMM: out[M, N] = round_to(gemm_dtype)(x_codes @ w_codesᵀ
  * decoded and scaled, as tfo_fp8_gemm with b_layout TFO_B_NK) + bias[N], the sum
  * in fp32 and stored as out_dtype: exactly the reference's

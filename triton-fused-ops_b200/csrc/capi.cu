@@ -424,6 +424,67 @@ int tfo_fp8_linear(const void* x_codes, const void* w_codes, const float* x_scal
   return TFO_OK;
 }
 
+int tfo_fp8_compute_scale_rows(const void* x, int64_t rows, int64_t cols, int x_dtype, float* scales, void* stream) {
+  const char* fn = "tfo_fp8_compute_scale_rows";
+  if (!is_float_dtype(x_dtype)) return fail(TFO_ERR_DTYPE, std::string(fn) + ": x must be f16, bf16 or f32");
+  if (rows < 0 || cols <= 0) return fail(TFO_ERR_INVALID, std::string(fn) + ": bad shape");
+  if (rows == 0) return TFO_OK;
+  if (!x || !scales) return fail(TFO_ERR_INVALID, std::string(fn) + ": NULL pointer");
+  const cudaError_t e = row_scales_launch(x, rows, cols, x_dtype, scales, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFO_OK : cuda_fail(e, fn);
+}
+
+int tfo_fp8_quantize_rows(const void* x, int64_t rows, int64_t cols, int x_dtype, const float* scales, void* out,
+                          int out_dtype, void* stream) {
+  const char* fn = "tfo_fp8_quantize_rows";
+  if (!is_float_dtype(x_dtype)) return fail(TFO_ERR_DTYPE, std::string(fn) + ": x must be f16, bf16 or f32");
+  if (out_dtype != U8 && out_dtype != E4M3) return fail(TFO_ERR_DTYPE, std::string(fn) + ": out must be U8 or E4M3");
+  if (rows < 0 || cols <= 0) return fail(TFO_ERR_INVALID, std::string(fn) + ": bad shape");
+  if (rows == 0) return TFO_OK;
+  if (!x || !scales || !out) return fail(TFO_ERR_INVALID, std::string(fn) + ": NULL pointer");
+  const cudaError_t e = encode_rows_launch(x, rows, cols, x_dtype, scales, out, out_dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFO_OK : cuda_fail(e, fn);
+}
+
+int tfo_fp8_dequantize_rows(const void* q, int64_t rows, int64_t cols, int q_dtype, const float* scales, void* out,
+                            int out_dtype, void* stream) {
+  const char* fn = "tfo_fp8_dequantize_rows";
+  if (q_dtype != U8 && q_dtype != E4M3) return fail(TFO_ERR_DTYPE, std::string(fn) + ": codes must be U8 or E4M3");
+  if (!is_float_dtype(out_dtype)) return fail(TFO_ERR_DTYPE, std::string(fn) + ": out must be f16, bf16 or f32");
+  if (rows < 0 || cols <= 0) return fail(TFO_ERR_INVALID, std::string(fn) + ": bad shape");
+  if (rows == 0) return TFO_OK;
+  if (!q || !scales || !out) return fail(TFO_ERR_INVALID, std::string(fn) + ": NULL pointer");
+  const cudaError_t e = decode_rows_launch(q, rows, cols, q_dtype, scales, out, out_dtype, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFO_OK : cuda_fail(e, fn);
+}
+
+size_t tfo_fp8_gemm_scaled_workspace_bytes(int64_t M, int64_t N, int64_t K, int ab_dtype, int b_layout) {
+  return tfo_fp8_gemm_workspace_bytes(M, N, K, ab_dtype, b_layout) +
+         ((4 * static_cast<size_t>(std::max<int64_t>(0, M) + std::max<int64_t>(0, N)) + 255) / 256) * 256;
+}
+
+int tfo_fp8_gemm_scaled(const void* a, const void* b, const float* a_scales, int a_per_row, const float* b_scales,
+                        int b_per_col, void* c, int64_t M, int64_t N, int64_t K, int ab_dtype, int b_layout,
+                        int out_dtype, void* workspace, size_t workspace_bytes, void* stream) {
+  const char* fn = "tfo_fp8_gemm_scaled";
+  if (ab_dtype != U8 && ab_dtype != E4M3) return fail(TFO_ERR_DTYPE, std::string(fn) + ": operands must be U8 or E4M3");
+  if (!is_float_dtype(out_dtype)) return fail(TFO_ERR_DTYPE, std::string(fn) + ": output must be f16, bf16 or f32");
+  if (b_layout != TFO_B_KN && b_layout != TFO_B_NK) return fail(TFO_ERR_INVALID, std::string(fn) + ": bad b_layout");
+  if (M < 0 || N < 0 || K <= 0) return fail(TFO_ERR_INVALID, std::string(fn) + ": bad dimension (K must be positive)");
+  if (M > INT32_MAX || N > INT32_MAX || K > 131072)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": M, N must fit in int32 and K <= 131072");
+  if (M == 0 || N == 0) return TFO_OK;
+  if (!a || !b || !a_scales || !b_scales || !c) return fail(TFO_ERR_INVALID, std::string(fn) + ": NULL pointer");
+  Fp8GemmArgs g{a, b, a_scales, b_scales, c, M, N, K, ab_dtype, b_layout, out_dtype, workspace, workspace_bytes};
+  g.sa_rows = a_per_row ? a_scales : nullptr;
+  g.sb_cols = b_per_col ? b_scales : nullptr;
+  if (!a_per_row && !b_per_col) g.sa_rows = nullptr;
+  if (!workspace || workspace_bytes < tfo_fp8_gemm_scaled_workspace_bytes(M, N, K, ab_dtype, b_layout))
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": workspace smaller than tfo_fp8_gemm_scaled_workspace_bytes()");
+  const cudaError_t e = fp8_gemm_launch(g, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFO_OK : cuda_fail(e, fn);
+}
+
 size_t tfo_gated_mlp_workspace_bytes(int64_t M, int64_t N, int64_t K, int x_dtype, int w_dtype) {
   if (M <= 0 || N <= 0 || K <= 0) return 0;
   GatedMlpArgs g{};

@@ -110,6 +110,12 @@ cudaError_t encode_launch(const void* x, int64_t n, int x_dtype, const float* sc
                           int nparts, float* scale_out, void* out, int out_dtype, cudaStream_t st);
 cudaError_t dequantize_launch(const void* q, int64_t n, int q_dtype, const float* scale, void* out, int out_dtype,
                               cudaStream_t st);
+// Per-row (per-token / per-channel) scales of a [rows, cols] matrix.
+cudaError_t row_scales_launch(const void* x, int64_t rows, int64_t cols, int x_dtype, float* scales, cudaStream_t st);
+cudaError_t encode_rows_launch(const void* x, int64_t rows, int64_t cols, int x_dtype, const float* scales, void* out,
+                               int out_dtype, cudaStream_t st);
+cudaError_t decode_rows_launch(const void* q, int64_t rows, int64_t cols, int q_dtype, const float* scales, void* out,
+                               int out_dtype, cudaStream_t st);
 // Workspace of the one-kernel dynamic-scale quantize: a barrier word at byte
 // 0 (zeroed by quantize_dynamic_launch) and one amax partial per CTA from
 // byte 256.
@@ -133,6 +139,9 @@ struct Fp8GemmArgs {
   const void* bias = nullptr;
   int bias_dtype = -1;
   int round_dtype = -1;
+  // per-token / per-channel scales: sa_rows[M] replaces sa, sb_cols[N] replaces sb
+  const float* sa_rows = nullptr;
+  const float* sb_cols = nullptr;
 };
 size_t fp8_gemm_workspace_bytes(const Fp8GemmArgs& g);
 // Launch choice of tfo_fp8_gemm for 16-byte-aligned operands: out = {rows

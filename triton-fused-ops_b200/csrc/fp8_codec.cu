@@ -370,6 +370,67 @@ __global__ void __launch_bounds__(kResThreads, 1)
   }
 }
 
+// ---- per-row (per-token / per-channel) scales ------------------------------
+// One warp per row of a [rows, cols] matrix (row-major, contiguous).
+constexpr int kRowThreads = 256;
+
+// scales[r] = 448 / max|x[r, :]| as FP8Format.compute_scale_per_channel
+// (triton_ops/models.py:301-314) evaluates it in torch: a zero max counts as
+// 1, and `448.0 / t` is `t.reciprocal() * 448`, each step rounded to x's dtype
+// (computed in fp32 first). The value is stored as fp32.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) row_scales_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+                                                                 float* __restrict__ scales) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x) >> 5; r < rows;
+       r += (static_cast<int64_t>(gridDim.x) * kRowThreads) >> 5) {
+    uint32_t m = 0;
+    const T* xr = x + r * cols;
+    for (int64_t c = lane; c < cols; c += 32) m = max(m, __float_as_uint(fabsf(Ty<T>::to_f(xr[c]))));
+    m = warp_max_u32(m);
+    if (lane == 0) {
+      const float amax = __uint_as_float(m);
+      const float rcp = Ty<T>::to_f(Ty<T>::from_f(__frcp_rn(amax == 0.f ? 1.0f : amax)));
+      scales[r] = Ty<T>::to_f(Ty<T>::from_f(__fmul_rn(rcp, 448.0f)));
+    }
+  }
+}
+
+// Codes of x[r, c] * scales[r] (reference codec: clamp, NaN kept; or e4m3).
+template <typename T, bool E4M3>
+__global__ void __launch_bounds__(kRowThreads) encode_rows_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+                                                                  const float* __restrict__ scales,
+                                                                  uint8_t* __restrict__ out) {
+  const int64_t n = rows * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * kRowThreads) {
+    const float c = __fmul_rn(Ty<T>::to_f(x[i]), __ldg(scales + i / cols));
+    out[i] = static_cast<uint8_t>(E4M3 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(c, __NV_SATFINITE, __NV_E4M3))
+                                       : ref_encode(c));
+  }
+}
+
+// out[r, c] = dec(q[r, c]) / scales[r], dec as in the per-tensor decode.
+template <typename TO, bool E4M3>
+__global__ void __launch_bounds__(kRowThreads) decode_rows_kernel(const uint8_t* __restrict__ q, int64_t rows,
+                                                                  int64_t cols, const float* __restrict__ scales,
+                                                                  TO* __restrict__ out) {
+  __shared__ float dec[256];
+  for (int u = threadIdx.x; u < 256; u += kRowThreads) {
+    if constexpr (E4M3) {
+      __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(u), __NV_E4M3);
+      dec[u] = __half2float(__half(hr));
+    } else {
+      dec[u] = __fmul_rn(__fdiv_rn(static_cast<float>(u - 128), 127.0f), 448.0f);
+    }
+  }
+  __syncthreads();
+  const int64_t n = rows * cols;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * kRowThreads)
+    out[i] = Ty<TO>::from_f(__fdiv_rn(dec[q[i]], __ldg(scales + i / cols)));
+}
+
 // ---- decode ----------------------------------------------------------------
 constexpr int kDecThreads = 512;
 
@@ -649,6 +710,61 @@ cudaError_t dequantize_launch(const void* q, int64_t n, int q_dtype, const float
     case F16: return dec_t<__half>(q, n, e4m3, scale, out, st);
     case BF16: return dec_t<__nv_bfloat16>(q, n, e4m3, scale, out, st);
     default: return dec_t<float>(q, n, e4m3, scale, out, st);
+  }
+}
+
+namespace {
+int rows_grid(int64_t work) { return grid_for(std::max<int64_t>(work, 1), kRowThreads, 8); }
+}  // namespace
+
+cudaError_t row_scales_launch(const void* x, int64_t rows, int64_t cols, int x_dtype, float* scales, cudaStream_t st) {
+  const int grid = rows_grid(rows * 32);
+  switch (x_dtype) {
+    case F16: row_scales_kernel<__half><<<grid, kRowThreads, 0, st>>>(static_cast<const __half*>(x), rows, cols, scales); break;
+    case BF16: row_scales_kernel<__nv_bfloat16><<<grid, kRowThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, scales); break;
+    default: row_scales_kernel<float><<<grid, kRowThreads, 0, st>>>(static_cast<const float*>(x), rows, cols, scales); break;
+  }
+  note_launch();
+  return cudaGetLastError();
+}
+
+template <typename T>
+static cudaError_t enc_rows_t(const void* x, int64_t rows, int64_t cols, const float* scales, void* out, bool e4m3,
+                              cudaStream_t st) {
+  const int grid = rows_grid(rows * cols);
+  if (e4m3) encode_rows_kernel<T, true><<<grid, kRowThreads, 0, st>>>(static_cast<const T*>(x), rows, cols, scales, static_cast<uint8_t*>(out));
+  else encode_rows_kernel<T, false><<<grid, kRowThreads, 0, st>>>(static_cast<const T*>(x), rows, cols, scales, static_cast<uint8_t*>(out));
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t encode_rows_launch(const void* x, int64_t rows, int64_t cols, int x_dtype, const float* scales, void* out,
+                               int out_dtype, cudaStream_t st) {
+  const bool e4 = out_dtype == E4M3;
+  switch (x_dtype) {
+    case F16: return enc_rows_t<__half>(x, rows, cols, scales, out, e4, st);
+    case BF16: return enc_rows_t<__nv_bfloat16>(x, rows, cols, scales, out, e4, st);
+    default: return enc_rows_t<float>(x, rows, cols, scales, out, e4, st);
+  }
+}
+
+template <typename TO>
+static cudaError_t dec_rows_t(const void* q, int64_t rows, int64_t cols, bool e4m3, const float* scales, void* out,
+                              cudaStream_t st) {
+  const int grid = rows_grid(rows * cols);
+  if (e4m3) decode_rows_kernel<TO, true><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, scales, static_cast<TO*>(out));
+  else decode_rows_kernel<TO, false><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, scales, static_cast<TO*>(out));
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t decode_rows_launch(const void* q, int64_t rows, int64_t cols, int q_dtype, const float* scales, void* out,
+                               int out_dtype, cudaStream_t st) {
+  const bool e4 = q_dtype == E4M3;
+  switch (out_dtype) {
+    case F16: return dec_rows_t<__half>(q, rows, cols, e4, scales, out, st);
+    case BF16: return dec_rows_t<__nv_bfloat16>(q, rows, cols, e4, scales, out, st);
+    default: return dec_rows_t<float>(q, rows, cols, e4, scales, out, st);
   }
 }
 

@@ -210,6 +210,8 @@ struct Fp8Epi {
     uint32_t* partial;  // split-K: [splits][M][N] raw accumulators
     const void* bias;   // FP8Linear: bias[N] of dtype bias_dt, added after rounding to round_dt
     int bias_dt, round_dt;
+    const float* ra;    // per-row factors codec_k / sa[m] (replace alpha when set, with rb)
+    const float* rb;    // per-column factors 1 / sb[n]
   };
   // alpha = fp32(codec_k / (sa * sb)), computed once per thread
   struct State {
@@ -249,6 +251,15 @@ struct Fp8Epi {
     }
     const float alpha = st.alpha;
     float v[16];
+    float colf[16];  // per-element factor: alpha, or ra[row] * rb[col]
+    if (p.ra != nullptr) {
+      const float rr = __ldg(p.ra + row);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) colf[i] = rr * __ldg(p.rb + min(col0 + i, N - 1));
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) colf[i] = alpha;
+    }
     if constexpr (INT_ACC) {
       int32_t cc[16];
       const int32_t cr = p.corr_row ? 128 * __ldg(p.corr_row + row) : 0;
@@ -266,15 +277,26 @@ struct Fp8Epi {
       }
 #pragma unroll
       for (int i = 0; i < 16; ++i)
-        v[i] = static_cast<float>(static_cast<int32_t>(r[0][i]) - cr - 128 * cc[i]) * alpha;
+        v[i] = static_cast<float>(static_cast<int32_t>(r[0][i]) - cr - 128 * cc[i]) * colf[i];
     } else {
 #pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[0][i]) * alpha;
+      for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[0][i]) * colf[i];
     }
     if (p.bias != nullptr) linear_bias16(v, p.bias, p.bias_dt, p.round_dt, col0, valid);
     store_row16<TO>(p.out + static_cast<int64_t>(row) * p.ldc + col0, v, valid, p.vec_ok);
   }
 };
+
+// Per-token / per-channel factors: ra[m] = codec_k / sa[m] (or / sa), rb[n] = 1 / sb[n] (or 1 / sb).
+__global__ void fp8_scale_vectors_kernel(const float* __restrict__ sa, const float* __restrict__ sa_rows,
+                                         const float* __restrict__ sb, const float* __restrict__ sb_cols, int64_t M,
+                                         int64_t N, double codec_k, float* __restrict__ ra, float* __restrict__ rb) {
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < M + N;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    if (i < M) ra[i] = static_cast<float>(codec_k / static_cast<double>(sa_rows != nullptr ? sa_rows[i] : *sa));
+    else rb[i - M] = static_cast<float>(1.0 / static_cast<double>(sb_cols != nullptr ? sb_cols[i - M] : *sb));
+  }
+}
 
 // Sums the split-K partials of each output, applies the correction and scale,
 // rounds to the output dtype.
@@ -285,7 +307,8 @@ __global__ void __launch_bounds__(256) fp8_splitk_finalize_kernel(const uint32_t
                                                                   const int32_t* __restrict__ corr_row,
                                                                   const int32_t* __restrict__ corr_col,
                                                                   const void* __restrict__ bias, int bias_dt,
-                                                                  int round_dt, TO* __restrict__ out) {
+                                                                  int round_dt, const float* __restrict__ ra,
+                                                                  const float* __restrict__ rb, TO* __restrict__ out) {
   const float alpha = static_cast<float>(codec_k / (static_cast<double>(__ldg(sa)) * __ldg(sb)));
   const int64_t total = M * N;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -302,7 +325,7 @@ __global__ void __launch_bounds__(256) fp8_splitk_finalize_kernel(const uint32_t
       for (int s = 0; s < splits; ++s) acc += __uint_as_float(partial[s * total + i]);
       v = acc;
     }
-    float r = v * alpha;
+    float r = v * (ra != nullptr ? ra[i / N] * rb[i % N] : alpha);
     if (bias != nullptr) r = __fadd_rn(round_to_dtype(r, round_dt), load_as_float(bias, i % N, bias_dt));
     out[i] = Ty<TO>::from_f(r);
   }
@@ -332,7 +355,7 @@ struct Fp8Plan {
   int64_t Kp;
   bool prep_a, prep_b;  // legacy: both; direct + codec: exactly one
   bool b_mn;            // B read MN-major from [K, N]
-  size_t off_a, off_b, off_sum, off_part, bytes;
+  size_t off_a, off_b, off_sum, off_part, off_vec, bytes;
   int bn, cg, splits;
   bool ksplit_cluster;  // K slices of a tile reduced inside one cluster (no partials, no finalize)
 };
@@ -387,6 +410,8 @@ Fp8Plan plan_fp8(const Fp8GemmArgs& g, bool assume_aligned) {
   pick_tiles(g.M, g.N, p.Kp, p);
   p.off_part = off;
   if (p.splits > 1 && !p.ksplit_cluster) off += round_up(static_cast<int64_t>(p.splits) * g.M * g.N * 4, 256);
+  p.off_vec = off;
+  if (g.sa_rows != nullptr || g.sb_cols != nullptr) off += round_up(4 * (g.M + g.N), 256);
   p.bytes = off;
   return p;
 }
@@ -395,6 +420,12 @@ template <MmaKind KIND, int BN, typename TO, bool B_MN, int CG>
 cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, const Fp8Plan& p,
                             uint32_t idesc, const int32_t* corr_row, const int32_t* corr_col, uint32_t* partial,
                             cudaStream_t st) {
+  const float* ra = nullptr;
+  const float* rb = nullptr;
+  if (g.sa_rows != nullptr || g.sb_cols != nullptr) {
+    ra = reinterpret_cast<const float*>(static_cast<uint8_t*>(g.ws) + p.off_vec);
+    rb = ra + g.M;
+  }
   constexpr int STAGES = (CG == 2) ? kStagesPair : kStages;
   using L = GemmLayout<BN, 1, STAGES, CG>;
   constexpr bool INT_ACC = (KIND == MmaKind::I8);
@@ -405,7 +436,7 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
   const double codec_k = INT_ACC ? (448.0 / 127.0) * (448.0 / 127.0) : 1.0;
   typename Epi::Params ep{static_cast<TO*>(g.c), g.sa, g.sb, codec_k, g.N,
                           al16(g.c) && (g.N * sizeof(TO)) % 16 == 0, corr_row, corr_col,
-                          p.splits > 1 ? partial : nullptr, g.bias, g.bias_dtype, g.round_dtype};
+                          p.splits > 1 ? partial : nullptr, g.bias, g.bias_dtype, g.round_dtype, ra, rb};
   const int64_t work = ((g.M + L::PAIR_M - 1) / L::PAIR_M) * ((g.N + BN - 1) / BN) * p.splits;
   if constexpr (CG == 1 && BN == 128) {
     if (p.ksplit_cluster) {
@@ -433,7 +464,7 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
   const int fgrid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((total + 255) / 256, num_sms() * 8)));
   fp8_splitk_finalize_kernel<TO, INT_ACC><<<fgrid, 256, 0, st>>>(partial, p.splits, g.M, g.N, g.sa, g.sb, codec_k,
                                                                  corr_row, corr_col, g.bias, g.bias_dtype,
-                                                                 g.round_dtype, static_cast<TO*>(g.c));
+                                                                 g.round_dtype, ra, rb, static_cast<TO*>(g.c));
   note_launch();
   return cudaGetLastError();
 }
@@ -552,6 +583,13 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
     b = reinterpret_cast<const uint8_t*>(db);
     corr_col = sums;
     a_fmt = 0;  // A stays raw u8
+  }
+  if (g.sa_rows != nullptr || g.sb_cols != nullptr) {
+    float* ra = reinterpret_cast<float*>(ws + p.off_vec);
+    const double codec_k = codec ? (448.0 / 127.0) * (448.0 / 127.0) : 1.0;
+    const int grid = static_cast<int>(std::min<int64_t>((g.M + g.N + 255) / 256, num_sms() * 4));
+    fp8_scale_vectors_kernel<<<grid, 256, 0, st>>>(g.sa, g.sa_rows, g.sb, g.sb_cols, g.M, g.N, codec_k, ra, ra + g.M);
+    note_launch();
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;

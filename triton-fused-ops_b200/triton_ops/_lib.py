@@ -69,6 +69,15 @@ _SIGNATURES = {
     "tfo_fp8_quantize": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_size, _c_vp]),
     "tfo_fp8_quantize_noalloc": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_int, _c_vp]),
     "tfo_fp8_dequantize": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_int, _c_vp]),
+    "tfo_fp8_compute_scale_rows": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp]),
+    "tfo_fp8_quantize_rows": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_int, _c_vp]),
+    "tfo_fp8_dequantize_rows": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_int, _c_vp]),
+    "tfo_fp8_gemm_scaled_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64, _c_int, _c_int]),
+    "tfo_fp8_gemm_scaled": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_vp,
+         _c_size, _c_vp],
+    ),
     "tfo_fp8_gemm_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64, _c_int, _c_int]),
     "tfo_fp8_gemm": (
         _c_int,

@@ -51,6 +51,8 @@ def _gemm_codes(a, b, a_scale, b_scale, output_dtype, b_layout):
     c = torch.empty(M, N, dtype=output_dtype, device=a.device)
     if c.numel() == 0:
         return c
+    if a_scale.numel() > 1 or b_scale.numel() > 1:
+        return _gemm_scaled(a, b, a_scale, b_scale, c, M, N, K, code, b_layout, output_dtype)
     sa = _scale_f32(a_scale.to(a.device))
     sb = _scale_f32(b_scale.to(a.device))
     lib = _lib.load()
@@ -59,6 +61,26 @@ def _gemm_codes(a, b, a_scale, b_scale, output_dtype, b_layout):
     _lib.call(
         "tfo_fp8_gemm", a.data_ptr(), b.data_ptr(), sa.data_ptr(), sb.data_ptr(), c.data_ptr(), M, N, K, code,
         b_layout, _lib.dtype_code(output_dtype, "output_dtype"), ws.data_ptr(), ws.numel(), _lib.stream_of(a),
+    )
+    return c
+
+
+def _gemm_scaled(a, b, a_scale, b_scale, c, M, N, K, code, b_layout, output_dtype):
+    """Per-token A scales (M values) and/or per-channel B scales (N values) in the epilogue."""
+    dev = a.device
+    a_rows = a_scale.numel() > 1
+    b_cols = b_scale.numel() > 1
+    if a_rows and a_scale.numel() != M:
+        raise ValueError(f"a_scale must hold 1 or M={M} values, got {a_scale.numel()}")
+    if b_cols and b_scale.numel() != N:
+        raise ValueError(f"b_scale must hold 1 or N={N} values, got {b_scale.numel()}")
+    sa = a_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    sb = b_scale.to(device=dev, dtype=torch.float32).reshape(-1).contiguous()
+    ws = _lib.workspace(_lib.load().tfo_fp8_gemm_scaled_workspace_bytes(M, N, K, code, b_layout), dev)
+    _lib.call(
+        "tfo_fp8_gemm_scaled", a.data_ptr(), b.data_ptr(), sa.data_ptr(), int(a_rows), sb.data_ptr(), int(b_cols),
+        c.data_ptr(), M, N, K, code, b_layout, _lib.dtype_code(output_dtype, "output_dtype"), ws.data_ptr(),
+        ws.numel(), _lib.stream_of(a),
     )
     return c
 

@@ -11,6 +11,10 @@ bytes of ``clamp(x*s, +-448)``.
 ``dequantize_fp8`` inverts either encoding: ``out = dec(q) / s``
 (reference: :176-211, oracle :290-312).
 
+Both also accept a scale with one value per row of the last dimension
+(shape ``[..., 1]``: per-token activations, per-output-channel ``[out, in]``
+weights), an extension: the reference's kernels read a single scale.
+
 The ``*_reference`` functions are plain-PyTorch restatements of the
 reference's oracles, kept importable for tests; the ops never call them.
 """
@@ -33,6 +37,19 @@ dequantize_fp8_kernel = NativeKernel("dequantize_fp8_kernel", "tfo_fp8_dequantiz
 compute_scale_kernel = NativeKernel("compute_scale_kernel", "tfo_fp8_compute_scale", "grid-wide amax -> scale")
 
 _CODE_DTYPES = (torch.uint8,) + ((torch.float8_e4m3fn,) if hasattr(torch, "float8_e4m3fn") else ())
+
+
+def _row_scales(tensor: torch.Tensor, scale: torch.Tensor):
+    """The per-row scale vector (fp32, contiguous) if `scale` holds one value per row of
+    `tensor` viewed as [numel / last_dim, last_dim] (shape [..., 1] or [rows]); else None."""
+    if scale is None or scale.numel() <= 1 or tensor.dim() < 1:
+        return None
+    cols = tensor.shape[-1]
+    rows = tensor.numel() // max(cols, 1)
+    if scale.numel() != rows or (scale.dim() == tensor.dim() and scale.shape[-1] != 1):
+        raise ValueError(f"a scale tensor must hold one value per row ({rows}) of the last dimension, "
+                         f"got shape {tuple(scale.shape)}")
+    return scale.to(device=tensor.device, dtype=torch.float32).reshape(rows).contiguous()
 
 
 def _scale_f32(scale: torch.Tensor) -> torch.Tensor:
@@ -81,6 +98,13 @@ def quantize_fp8(
         return out, scale
     if scale.device != dev:
         scale = scale.to(dev)
+    rs = _row_scales(tensor, scale)
+    if rs is not None:
+        # per-token / per-channel scales: one multiplier per row of the last dimension
+        if n:
+            _lib.call("tfo_fp8_quantize_rows", tensor.data_ptr(), rs.numel(), tensor.shape[-1], x_code, rs.data_ptr(),
+                      out.data_ptr(), out_code, stream)
+        return out, scale
     s32 = _scale_f32(scale)
     if n:
         _lib.call("tfo_fp8_quantize", tensor.data_ptr(), n, x_code, s32.data_ptr(), None, out.data_ptr(),
@@ -110,6 +134,11 @@ def dequantize_fp8(
     q = tensor.contiguous()
     n = q.numel()
     if n:
+        rs = _row_scales(q, scale)
+        if rs is not None:
+            _lib.call("tfo_fp8_dequantize_rows", q.data_ptr(), rs.numel(), q.shape[-1], _lib.dtype_code(q.dtype),
+                      rs.data_ptr(), out.data_ptr(), _lib.dtype_code(output_dtype), _lib.stream_of(q))
+            return out
         s32 = _scale_f32(scale.to(tensor.device))
         _lib.call("tfo_fp8_dequantize", q.data_ptr(), n, _lib.dtype_code(q.dtype), s32.data_ptr(), out.data_ptr(),
                   _lib.dtype_code(output_dtype), _lib.stream_of(q))

@@ -198,7 +198,24 @@ class FP8Format:
 
     @staticmethod
     def compute_scale_per_channel(tensor: torch.Tensor, dim: int = 0) -> torch.Tensor:
-        """Per-channel multipliers ``448 / max|x|`` along `dim` (1 where the max is 0)."""
+        """Per-channel multipliers ``448 / max|x|`` along `dim` (1 where the max is 0).
+
+        Reducing over the last dimension of a contiguous CUDA tensor (``dim=-1``:
+        per token of activations, per output channel of an ``[out, in]`` weight)
+        runs the library's kernel (``tfo_fp8_compute_scale_rows``), which
+        rounds like the torch expression below (``448.0 / t`` is
+        ``t.reciprocal() * 448`` in the tensor's dtype) and returns the same
+        values, dtype and ``[..., 1]`` shape.
+        """
+        if (tensor.is_cuda and tensor.is_contiguous() and tensor.dim() >= 1 and tensor.numel() > 0
+                and dim in (-1, tensor.dim() - 1) and tensor.dtype in (torch.float16, torch.bfloat16, torch.float32)):
+            from triton_ops import _lib
+
+            cols = tensor.shape[-1]
+            out = torch.empty(*tensor.shape[:-1], 1, dtype=torch.float32, device=tensor.device)
+            _lib.call("tfo_fp8_compute_scale_rows", tensor.data_ptr(), tensor.numel() // cols, cols,
+                      _lib.dtype_code(tensor.dtype), out.data_ptr(), _lib.stream_of(tensor))
+            return out if tensor.dtype == torch.float32 else out.to(tensor.dtype)
         max_abs = tensor.abs().amax(dim=dim, keepdim=True)
         max_abs = torch.where(max_abs == 0, torch.ones_like(max_abs), max_abs)
         return FP8Format.max_value / max_abs
