@@ -116,9 +116,8 @@ cudaError_t encode_rows_launch(const void* x, int64_t rows, int64_t cols, int x_
                                int out_dtype, cudaStream_t st);
 cudaError_t decode_rows_launch(const void* q, int64_t rows, int64_t cols, int q_dtype, const float* scales, void* out,
                                int out_dtype, cudaStream_t st);
-// Workspace of the one-kernel dynamic-scale quantize: a barrier word at byte
-// 0 (zeroed by quantize_dynamic_launch) and one amax partial per CTA from
-// byte 256.
+// Workspace of the one-kernel dynamic-scale quantize: a grid-barrier counter
+// and the running max at bytes 0-7 (zeroed by quantize_dynamic_launch).
 size_t quantize_dynamic_workspace_bytes();
 cudaError_t quantize_dynamic_launch(const void* x, int64_t n, int x_dtype, float* scale_out, void* out, int out_dtype,
                                     void* ws, size_t ws_bytes, cudaStream_t st);

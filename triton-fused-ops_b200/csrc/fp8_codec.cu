@@ -194,14 +194,14 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const T* __restrict
 }
 
 // ---- dynamic-scale quantize in one kernel ----------------------------------
-// Cooperative launch (all CTAs resident). Pass 1: each CTA's max |x| goes to
-// partials[blockIdx]; CTAs then meet at a grid barrier, a counter in the
-// workspace that the host zeroes before the launch and every CTA increments
-// once. Pass 2: every CTA reduces the partials to the scale (CTA 0 publishes
-// it) and encodes the same elements it read in pass 1, which for tensors up
-// to the L2 size come back from L2 rather than HBM. The barrier wait is
-// bounded: on expiry the CTA sets ERR_GRID_BARRIER and returns without
-// writing its share of the output.
+// Cooperative launch (all CTAs resident). Pass 1: each CTA folds its max |x|
+// into one global word and arrives on a counter (both in the workspace,
+// zeroed by the host before the launch); after the grid barrier every CTA
+// reads the max, derives the scale (CTA 0 publishes it) and, in pass 2,
+// encodes the same elements it read in pass 1, which for tensors up to the L2
+// size come back from L2 rather than HBM. The barrier wait is bounded: on
+// expiry the CTA sets ERR_GRID_BARRIER and returns without writing its share
+// of the output.
 constexpr int kQuantThreads = 512;
 
 __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
@@ -210,15 +210,16 @@ __device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
   return v;
 }
 
-// Publishes this CTA's partial max and waits (bounded) until every CTA of the
-// grid has published; then returns the scale reduced from all partials (every
-// CTA computes the same value). Returns false if the wait ran out of budget
-// (ERR_GRID_BARRIER is set and the caller must not write its output).
-__device__ __forceinline__ bool grid_publish_and_scale(uint32_t b, uint32_t* __restrict__ barrier,
-                                                       uint32_t* __restrict__ partials, uint32_t* __restrict__ err,
-                                                       uint32_t* red, float* s_sh, int* ok_sh) {
+// Grid-wide max and scale with a single global word: every CTA folds its max
+// into barrier[1] (atomicMax on the bits of a non-negative float orders like
+// the value, NaN above inf), then arrives on the counter barrier[0]; both
+// words are zeroed by the host before the launch. After the (bounded) wait one
+// load gives the max. Returns false if the wait ran out of budget
+// (ERR_GRID_BARRIER set; the caller must not write its output).
+__device__ __forceinline__ bool grid_max_scale(uint32_t b, uint32_t* __restrict__ barrier, uint32_t* __restrict__ err,
+                                               float* s_sh, int* ok_sh) {
   if (threadIdx.x == 0) {
-    partials[blockIdx.x] = b;
+    atomicMax(barrier + 1, b);
     __threadfence();
     atomicAdd(barrier, 1u);
     int ok = 1;
@@ -230,24 +231,20 @@ __device__ __forceinline__ bool grid_publish_and_scale(uint32_t b, uint32_t* __r
           ok = 0;
           break;
         }
-        __nanosleep(128);
+        __nanosleep(32);
       }
     }
-    __threadfence();
     *ok_sh = ok;
+    *s_sh = scale_from_amax(ld_acquire_gpu(barrier + 1));
   }
   __syncthreads();
-  if (!*ok_sh) return false;
-  const float s = reduce_partials_to_scale(partials, gridDim.x, red);
-  if (threadIdx.x == 0) *s_sh = s;
-  __syncthreads();
-  return true;
+  return *ok_sh != 0;
 }
 
 template <typename T, bool E4M3>
 __global__ void __launch_bounds__(kQuantThreads, 2)
     quantize_dynamic_kernel(const T* __restrict__ x, int64_t n, bool vec, uint32_t* __restrict__ barrier,
-                            uint32_t* __restrict__ partials, float* __restrict__ scale_out,
+                            float* __restrict__ scale_out,
                             uint8_t* __restrict__ out, uint32_t* __restrict__ err) {
   __shared__ uint32_t red[32];
   __shared__ float s_sh;
@@ -255,7 +252,7 @@ __global__ void __launch_bounds__(kQuantThreads, 2)
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   const uint32_t b = block_max_u32(amax_share<T, 4>(x, n, vec, tid, stride), red);
-  if (!grid_publish_and_scale(b, barrier, partials, err, red, &s_sh, &ok_sh)) return;
+  if (!grid_max_scale(b, barrier, err, &s_sh, &ok_sh)) return;
   const float sc = s_sh;
   if (threadIdx.x == 0 && blockIdx.x == 0) *scale_out = sc;
   if (sc > 0.f && sc < INFINITY) encode_share<T, E4M3, 2, true>(x, n, vec, sc, out, tid, stride);
@@ -271,13 +268,13 @@ __global__ void __launch_bounds__(kQuantThreads, 2)
 // of the codes. 16-byte vectors; the last CTA also covers the n % 16 tail
 // elements from global memory.
 constexpr int kResThreads = 1024;
-constexpr int kResPieces = 8;
+constexpr int kResPieces = 16;
 constexpr size_t kResSlabMax = 227 * 1024 - 1024;
 
 template <typename T, bool E4M3>
 __global__ void __launch_bounds__(kResThreads, 1)
     quantize_resident_kernel(const T* __restrict__ x, int64_t n, int64_t vecs_per_cta, uint32_t* __restrict__ barrier,
-                             uint32_t* __restrict__ partials, float* __restrict__ scale_out,
+                             float* __restrict__ scale_out,
                              uint8_t* __restrict__ out, uint32_t* __restrict__ err) {
   constexpr int EV = 16 / sizeof(T);  // elements per 16-byte vector
   extern __shared__ __align__(128) uint4 slab[];
@@ -318,7 +315,7 @@ __global__ void __launch_bounds__(kResThreads, 1)
     for (int64_t i = nvec * EV + threadIdx.x; i < n; i += kResThreads)
       mf = max(mf, __float_as_uint(fabsf(Ty<T>::to_f(x[i]))));
   const uint32_t bmax = block_max_u32(mf, red);
-  if (!grid_publish_and_scale(bmax, barrier, partials, err, red, &s_sh, &ok_sh)) return;
+  if (!grid_max_scale(bmax, barrier, err, &s_sh, &ok_sh)) return;
   const float s = s_sh;
   if (threadIdx.x == 0 && blockIdx.x == 0) *scale_out = s;
   const bool in_range = (s > 0.f && s < INFINITY);
@@ -587,8 +584,7 @@ cudaError_t quant_dyn_t(const void* x, int64_t n, float* scale_out, void* out, v
   const int grid = static_cast<int>(std::min<int64_t>(want, static_cast<int64_t>(occ) * num_sms()));
   if (ws_bytes < kQuantPartialsOffset + sizeof(uint32_t) * static_cast<size_t>(grid)) return cudaErrorInvalidValue;
   auto* barrier = static_cast<uint32_t*>(ws);
-  auto* partials = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + kQuantPartialsOffset);
-  cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(uint32_t), st);
+  cudaError_t e = cudaMemsetAsync(barrier, 0, 2 * sizeof(uint32_t), st);  // counter + max
   note_launch();
   if (e != cudaSuccess) return e;
   const T* xp = static_cast<const T*>(x);
@@ -605,7 +601,7 @@ cudaError_t quant_dyn_t(const void* x, int64_t n, float* scale_out, void* out, v
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kernel, xp, n, vec, barrier, partials, scale_out, op, err);
+  e = cudaLaunchKernelEx(&cfg, kernel, xp, n, vec, barrier, scale_out, op, err);
   note_launch();
   return e;
 }
@@ -637,8 +633,7 @@ cudaError_t quant_res_t(const void* x, int64_t n, float* scale_out, void* out, v
     attr_set[dev].store(true);
   }
   auto* barrier = static_cast<uint32_t*>(ws);
-  auto* partials = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + kQuantPartialsOffset);
-  cudaError_t e = cudaMemsetAsync(barrier, 0, sizeof(uint32_t), st);
+  cudaError_t e = cudaMemsetAsync(barrier, 0, 2 * sizeof(uint32_t), st);  // counter + max
   note_launch();
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -651,7 +646,7 @@ cudaError_t quant_res_t(const void* x, int64_t n, float* scale_out, void* out, v
   attr[0].val.cooperative = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kernel, static_cast<const T*>(x), n, vpc, barrier, partials, scale_out,
+  e = cudaLaunchKernelEx(&cfg, kernel, static_cast<const T*>(x), n, vpc, barrier, scale_out,
                          static_cast<uint8_t*>(out), error_word_ptr());
   note_launch();
   *used = true;
