@@ -124,6 +124,20 @@ int gemm_resident_units(const void* kernel, size_t smem, int cg) {
   return units;
 }
 
+cudaError_t ensure_smem_attr(const void* kernel, size_t smem) {
+  if (smem <= 48 * 1024) return cudaSuccess;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> done;
+  std::lock_guard<std::mutex> lk(mu);
+  size_t& have = done[std::make_pair(kernel, dev)];
+  if (have >= smem) return cudaSuccess;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess) have = smem;
+  return e;
+}
+
 size_t scale_workspace_bytes(int64_t numel) {
   return std::max(static_cast<size_t>(amax_partials_count(numel)) * sizeof(uint32_t),
                   quantize_dynamic_workspace_bytes());

@@ -23,6 +23,9 @@ uint32_t* error_word_ptr();
 int num_sms();
 // cudaOccupancyMaxActiveBlocksPerMultiprocessor, cached per (kernel, block, smem).
 int cached_occupancy(const void* kernel, int block, size_t smem);
+// Raises the kernel's dynamic shared-memory limit to at least `smem` bytes on
+// the current device; the attribute call is made once per (kernel, device, size).
+cudaError_t ensure_smem_attr(const void* kernel, size_t smem);
 // For a persistent GEMM kernel (192 threads, `smem` bytes of dynamic shared
 // memory, raised on first use): how many work units can be resident at once
 // on the current device, a unit being one CTA (cg == 1) or one cluster of two

@@ -622,16 +622,8 @@ cudaError_t quant_res_t(const void* x, int64_t n, float* scale_out, void* out, v
   const int grid = static_cast<int>((nvec + vpc - 1) / vpc);
   if (ws_bytes < kQuantPartialsOffset + sizeof(uint32_t) * static_cast<size_t>(grid)) return cudaErrorInvalidValue;
   auto kernel = quantize_resident_kernel<T, E4M3>;
-  static std::atomic<bool> attr_set[64];
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  if (!attr_set[dev].load()) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kernel),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kResSlabMax));
-    if (e != cudaSuccess) return e;
-    attr_set[dev].store(true);
-  }
+  if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), kResSlabMax); e != cudaSuccess)
+    return e;
   auto* barrier = static_cast<uint32_t*>(ws);
   cudaError_t e = cudaMemsetAsync(barrier, 0, 2 * sizeof(uint32_t), st);  // counter + max
   note_launch();

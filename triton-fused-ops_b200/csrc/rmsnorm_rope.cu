@@ -549,11 +549,7 @@ cudaError_t launch_vec(const RmsNormRopeArgs& a, int threads, cudaStream_t st) {
   // ring of up to 8 rows, about 32 KB, at least 2 (4 CTAs per SM at H = 4096 fp16)
   const int stages = std::max(2, std::min(8, (32 * 1024) / row_bytes));
   const size_t smem = vec_smem_bytes(static_cast<int>(a.hidden), row_bytes, stages);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-  }
+  if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem); e != cudaSuccess) return e;
   const int occ = cached_occupancy(reinterpret_cast<const void*>(kern), threads, smem);
   const int64_t rows = a.batch * a.seq_len;
   const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * std::max(occ, 1));
@@ -575,9 +571,7 @@ template <typename TX, typename TCS, bool FULLROT, int VPL, int MODE>
 cudaError_t launch_warp_rows_m(const RmsNormRopeArgs& a, int warps, int cs_stride, size_t smem, const RowQuantArgs& q,
                                cudaStream_t st) {
   auto kern = rmsnorm_rope_warp_kernel<TX, TCS, FULLROT, VPL, MODE>;
-  cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern), cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       static_cast<int>(smem));
-  if (e != cudaSuccess) return e;
+  if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem); e != cudaSuccess) return e;
   const int64_t rows = a.batch * a.seq_len;
   const int64_t grid = warp_rows_grid(rows, warps);
   kern<<<static_cast<unsigned>(grid), warps * 32, smem, st>>>(
@@ -665,11 +659,7 @@ cudaError_t launch_generic(const RmsNormRopeArgs& a, cudaStream_t st) {
   const int64_t rows = a.batch * a.seq_len;
   const size_t smem = static_cast<size_t>(a.hidden) * sizeof(float);
   auto kern = rmsnorm_rope_generic_kernel<TX>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(reinterpret_cast<const void*>(kern),
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    if (e != cudaSuccess) return e;
-  }
+  if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem); e != cudaSuccess) return e;
   const int occ = cached_occupancy(reinterpret_cast<const void*>(kern), 256, smem);
   const int64_t grid = std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * std::max(occ, 1));
   kern<<<static_cast<unsigned>(grid), 256, smem, st>>>(

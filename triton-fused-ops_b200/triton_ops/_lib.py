@@ -148,8 +148,13 @@ def dtype_code(dtype: torch.dtype, what: str = "tensor") -> int:
         ) from None
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_of(t: torch.Tensor) -> int:
-    """Raw handle of torch's current stream on t's device."""
+    """Raw handle of torch's current stream on t's device (no Stream object is built)."""
+    if _raw_stream is not None:
+        return _raw_stream(t.get_device())
     return torch.cuda.current_stream(t.device).cuda_stream
 
 
