@@ -385,6 +385,14 @@ __device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) {
 }
 
 // ---------------------------------------------------------------------------
+// Programmatic dependent launch: a kernel launched with
+// cudaLaunchAttributeProgrammaticStreamSerialization may start while the
+// previous kernel in the stream finishes; griddep_wait() blocks until that
+// kernel has completed and its memory is visible (a no-op otherwise).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------
 // misc
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {

@@ -215,6 +215,9 @@ __global__ void __launch_bounds__(192, 1)
   if constexpr (CG == 2) cluster_sync();  // the peer's barriers are initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  // everything above overlaps the previous kernel when launched as a
+  // programmatic dependent; global memory is touched only after this
+  griddep_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
