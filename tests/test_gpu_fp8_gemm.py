@@ -57,6 +57,32 @@ def test_integer_exactness(cuda):
         np.testing.assert_allclose(out, exact.astype(np.float64), rtol=2e-7, atol=0)
 
 
+@pytest.mark.parametrize("M,N,K,splits", [(16, 2048, 33 * 128, 8),   # one cluster per tile, slices of 4 and 5 K blocks
+                                          (16, 1024, 37 * 128, 9),   # partial sums + finalize, slices of 4 and 5
+                                          (100, 2048, 4096, 8)])
+def test_k_split_uneven_slices_exact(cuda, M, N, K, splits):
+    """K split into slices that differ by one K block; none may be empty (an empty slice would add stale TMEM)."""
+    from triton_ops import _lib, fp8_gemm
+
+    assert _lib.select_tile(_lib.OP_FP8_GEMM, M, N, K, _lib.U8)[4] == splits
+    rng = np.random.default_rng(M + N + K)
+    ua = rng.integers(1, 256, (M, K), dtype=np.uint8)
+    ub = rng.integers(1, 256, (K, N), dtype=np.uint8)
+    s = torch.tensor(448.0 / 127.0, device="cuda")
+    out = host(fp8_gemm(torch.from_numpy(ua).cuda(), torch.from_numpy(ub).cuda(), s, s, torch.float32))
+    exact = (ua.astype(np.int64) - 128) @ (ub.astype(np.int64) - 128)
+    assert np.abs(exact).max() < 2**24
+    np.testing.assert_allclose(out, exact.astype(np.float64), rtol=2e-7, atol=0)
+    # e4m3 operands: fp32 slice sums
+    a8 = torch.from_numpy(rng.standard_normal((M, K), dtype=np.float32)).cuda().to(torch.float8_e4m3fn)
+    b8 = torch.from_numpy(rng.standard_normal((K, N), dtype=np.float32)).cuda().to(torch.float8_e4m3fn)
+    one = torch.tensor(1.0, device="cuda")
+    out8 = host(fp8_gemm(a8, b8, one, one, torch.float32))
+    ref8 = a8.float().cpu().numpy().astype(np.float64) @ b8.float().cpu().numpy().astype(np.float64)
+    assert O.rel_fro(out8, ref8) <= 1e-5
+    assert _lib.device_error_flags() == 0
+
+
 @pytest.mark.parametrize("M", [16, 128, 1024])
 def test_config3_shapes(cuda, M):
     from triton_ops import fp8_gemm

@@ -336,8 +336,10 @@ __global__ void __launch_bounds__(256) fp8_splitk_finalize_kernel(const uint32_t
 // ---------------------------------------------------------------------------
 namespace {
 
-constexpr int kStages = 4;      // 48 KB stages (one CTA per MMA)
+constexpr int kStages = 4;      // 48 KB stages (one CTA per MMA, 256-column tiles)
+constexpr int kStages128 = 7;   // 32 KB stages (one CTA per MMA, 128-column tiles)
 constexpr int kStagesPair = 6;  // 32 KB stages (two CTAs per MMA)
+constexpr int stages_for(int bn, int cg) { return cg == 2 ? kStagesPair : (bn == 256 ? kStages : kStages128); }
 constexpr int kGroupM = 16;
 
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
@@ -426,7 +428,7 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
     ra = reinterpret_cast<const float*>(static_cast<uint8_t*>(g.ws) + p.off_vec);
     rb = ra + g.M;
   }
-  constexpr int STAGES = (CG == 2) ? kStagesPair : kStages;
+  constexpr int STAGES = stages_for(BN, CG);
   using L = GemmLayout<BN, 1, STAGES, CG>;
   constexpr bool INT_ACC = (KIND == MmaKind::I8);
   using Epi = Fp8Epi<TO, INT_ACC>;
@@ -440,9 +442,10 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
   const int64_t work = ((g.M + L::PAIR_M - 1) / L::PAIR_M) * ((g.N + BN - 1) / BN) * p.splits;
   if constexpr (CG == 1 && BN == 128) {
     if (p.ksplit_cluster) {
-      // one CTA per (tile, K slice); the slices of a tile form one cluster
-      using LK = GemmLayout<BN, 1, kStages, 1, true>;
-      auto kk = umma_gemm_kernel<KIND, BN, 1, kStages, Epi, B_MN, 1, true>;
+      // one CTA per (tile, K slice); the slices of a tile form one cluster and
+      // sum their raw tiles through distributed shared memory
+      using LK = GemmLayout<BN, 1, STAGES, 1, true>;
+      auto kk = umma_gemm_kernel<KIND, BN, 1, STAGES, Epi, B_MN, 1, true>;
       if (gemm_resident_units(reinterpret_cast<const void*>(kk), LK::SMEM_BYTES, 1) <= 0)
         return cudaErrorInvalidConfiguration;
       typename Epi::Params epk = ep;
@@ -513,7 +516,7 @@ void fp8_gemm_tile(int64_t M, int64_t N, int64_t K, int ab_dtype, int b_layout, 
   out[0] = 128 * p.cg;
   out[1] = p.bn;
   out[2] = p.cg;
-  out[3] = p.cg == 2 ? kStagesPair : kStages;
+  out[3] = stages_for(p.bn, p.cg);
   out[4] = p.splits;
   out[5] = kGroupM;
 }

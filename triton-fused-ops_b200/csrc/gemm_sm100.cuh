@@ -65,17 +65,24 @@ struct GemmLayout {
   static_assert(CG == 1 || (B_ROWS % 128 == 0 && (NUM_B == 1 || B_ROWS == BLOCK_N)),
                 "pair MMA: each CTA stages whole 128-row B boxes (one operand each when NUM_B == 2)");
   static_assert(!KSPLIT || (CG == 1 && NUM_B == 1), "cluster K split: one CTA per MMA, one B operand");
-  // cluster K split: the raw accumulator tile, read by the cluster's other CTAs
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  // cluster K split: the raw accumulator tile (read by the cluster's other
+  // CTAs) and the tile of this CTA's summed rows (at most half the rows, as
+  // k_splits >= 2). Both reuse the ring: a K-split CTA runs one work item,
+  // and once its accumulator is complete no TMA write or MMA read of the ring
+  // remains.
   static constexpr int RED_BYTES = KSPLIT ? BM * N_MMA * 4 : 0;
-  static constexpr int RED_OFFSET = STAGES * STAGE_BYTES;
-  static constexpr int BAR_OFFSET = RED_OFFSET + RED_BYTES;
-  // dynamic shared memory: ring + reduction tile + barriers + 1 KB for manual alignment
+  static constexpr int SUM_OFFSET = RED_BYTES;
+  static constexpr int SUM_BYTES = KSPLIT ? (BM / 2) * N_MMA * 4 : 0;
+  static_assert(RED_BYTES + SUM_BYTES <= RING_BYTES, "reduction tiles fit in the ring");
+  static constexpr int BAR_OFFSET = RING_BYTES;
+  // dynamic shared memory: ring + barriers + 1 KB for manual alignment
   static constexpr size_t SMEM_BYTES = static_cast<size_t>(BAR_OFFSET) + 256 + 1024;
 };
 
-// Address of 16-byte vector `v` of accumulator row `row` in the reduction
-// tile (N_MMA / 4 vectors per row, XOR-swizzled by row so that the 32 rows of
-// a warp spread over all banks).
+// Address of 16-byte vector `v` of row `row` in a K-split reduction tile
+// (VECS_PER_ROW vectors per row, XOR-swizzled by row: a warp storing one
+// vector of 32 rows, or reading 16 columns of 4 rows, spreads over all banks).
 template <int VECS_PER_ROW>
 __device__ __forceinline__ int red_vec_index(int row, int v) {
   return row * VECS_PER_ROW + (v ^ (row & 7));
@@ -89,6 +96,9 @@ __device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t cluster_addr) {
                : "memory");
   return r;
 }
+
+// Barrier 1 over the four epilogue warps (barrier 0 is __syncthreads).
+__device__ __forceinline__ void epilogue_warps_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 // Waits for `parity` on `bar`, giving up when the CTA abort flag is raised or
 // the budget runs out (then sets the error bit and raises the flag).
@@ -135,11 +145,15 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 //
 // KSPLIT: the k_splits K slices of a tile run as one cluster of k_splits CTAs
 // (one work item per CTA, grid = tiles x k_splits). Each CTA leaves its raw
-// accumulator tile in shared memory; after a cluster barrier CTA r sums rows
-// [r * 128 / k_splits, +128 / k_splits) over the cluster's tiles in slice
-// order (through distributed shared memory) and runs the epilogue on the sums
-// (Epi must provide add_partial and final_params); a second cluster barrier
-// keeps every tile readable until all CTAs are done.
+// accumulator tile (rows inside M) in shared memory over the drained ring.
+// After a cluster barrier CTA r takes the r-th of k_splits contiguous row
+// blocks of the tile's rows inside M: a warp reads one row of every slice's
+// tile through distributed shared memory (lane l: 16-byte vector l, so each
+// request is 512 contiguous bytes; four rows' requests in flight), sums the
+// slices in slice order into a local tile of sums, and after a barrier of
+// the epilogue warps the epilogue runs on 16-column units of that tile (Epi
+// must provide add_partial and final_params). A second cluster barrier keeps
+// every tile readable until all CTAs are done. 2 <= k_splits <= 8.
 template <MmaKind KIND, int BLOCK_N, int NUM_B, int STAGES, class Epi, bool B_MN = false, int CG = 1,
           bool KSPLIT = false>
 __global__ void __launch_bounds__(192, 1)
@@ -155,7 +169,6 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sa = smem;
   uint8_t* sb = smem + STAGES * L::A_BYTES;
-  uint4* red_tile = reinterpret_cast<uint4*>(smem + L::RED_OFFSET);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -171,8 +184,8 @@ __global__ void __launch_bounds__(192, 1)
   const int num_tiles = sched.num_tiles();
   const int num_k = (K + KB_ELEMS - 1) / KB_ELEMS;
   const int num_work = num_tiles * k_splits;
-  const int kb_per_split = (num_k + k_splits - 1) / k_splits;
-  // work item -> (tile, K-block range, slice)
+  // work item -> (tile, K-block range, slice); slices differ by at most one
+  // K block, so none is empty while k_splits <= num_k (the host's split rule)
   struct Work {
     int m_blk, n_blk, kb0, kb1, split;
   };
@@ -181,10 +194,18 @@ __global__ void __launch_bounds__(192, 1)
     const int tile = w / k_splits;
     r.split = w - tile * k_splits;
     sched.coords(tile, r.m_blk, r.n_blk);
-    r.kb0 = r.split * kb_per_split;
-    r.kb1 = min(num_k, r.kb0 + kb_per_split);
+    r.kb0 = static_cast<int>(static_cast<int64_t>(r.split) * num_k / k_splits);
+    r.kb1 = static_cast<int>(static_cast<int64_t>(r.split + 1) * num_k / k_splits);
     return r;
   };
+  uint4* red_tile = reinterpret_cast<uint4*>(smem);
+  if constexpr (KSPLIT) {
+    // the reduction tiles reuse the ring, which holds for one work item per CTA
+    if (static_cast<int>(gridDim.x) != num_work) {
+      if (threadIdx.x == 0) atomicOr(err, ERR_BAD_LAUNCH);
+      return;  // uniform over the grid: no CTA reaches a barrier
+    }
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -218,6 +239,9 @@ __global__ void __launch_bounds__(192, 1)
   // everything above overlaps the previous kernel when launched as a
   // programmatic dependent; global memory is touched only after this
   griddep_wait();
+  // epilogue state (a K split's final pass reuses it: its epilogue keeps no
+  // per-tile state)
+  typename Epi::State est{};
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -322,7 +346,7 @@ __global__ void __launch_bounds__(192, 1)
     const int sub = warp & 3;
     const int row_in_tile = static_cast<int>(rank) * L::BM + sub * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
-    typename Epi::State est = Epi::init(ep);
+    est = Epi::init(ep);
     int tcount = 0;
     for (int w = unit; w < num_work; w += num_units, ++tcount) {
       const int acc = tcount & 1;
@@ -334,6 +358,15 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t base = tmem_base + lane_addr + acc * L::ACC_COLS;
       // Two register sets: the TMEM load of the next 16 columns is in flight
       // while the current ones are converted and stored.
+      if (wk.m_blk * L::PAIR_M + row_in_tile - lane >= M) {
+        // all 32 rows of this warp lie past M: nothing to read or store
+        __syncwarp();
+        if (lane == 0) {
+          if constexpr (CG == 2) mbar_arrive_cluster(mapa_shared(smem_u32(&tempty[acc]), 0));
+          else mbar_arrive(&tempty[acc]);
+        }
+        continue;
+      }
       if constexpr (KSPLIT) {
         // raw accumulators to the reduction tile (row = this thread's TMEM lane)
         const int trow = sub * 32 + lane;
@@ -384,30 +417,63 @@ __global__ void __launch_bounds__(192, 1)
   if constexpr (KSPLIT) {
     cluster_sync();  // every slice's tile is in shared memory
     if (warp >= 2) {
-      typename Epi::State est = Epi::init(ep);
+      constexpr int VECS = L::N_MMA / 4;
+      constexpr int CHUNKS = BLOCK_N / 16;
+      constexpr int MAX_SPLITS = 8;
+      constexpr int ROWS_IN_FLIGHT = 4;
+      static_assert(VECS == 32, "one 16-byte vector of a row per lane");
       const typename Epi::Params epf = Epi::final_params(ep);
       const Work wk = work(blockIdx.x);
-      const int rows_per = (L::BM + k_splits - 1) / k_splits;
-      const int r0 = static_cast<int>(cluster_ctarank()) * rows_per;
-      const int nrows = max(0, min(L::BM, r0 + rows_per) - r0);
-      constexpr int CHUNKS = BLOCK_N / 16;
+      const int row0 = wk.m_blk * L::PAIR_M;
+      const int rows = max(0, min(L::BM, M - row0));
+      const int per = (rows + k_splits - 1) / k_splits;  // <= BM / 2 rows
+      const int r_begin = min(rows, static_cast<int>(cluster_ctarank()) * per);
+      const int r_end = min(rows, r_begin + per);
       const uint32_t tile_base = smem_u32(red_tile);
-      for (int u = threadIdx.x - 64; u < nrows * CHUNKS; u += 128) {
-        const int trow = r0 + u / CHUNKS, c = (u % CHUNKS) * 16;
-        const int row = wk.m_blk * L::PAIR_M + trow;
-        if (row >= M) continue;
-        uint32_t sum[1][16];
-        for (int sl = 0; sl < k_splits; ++sl) {
+      uint4* sum_tile = reinterpret_cast<uint4*>(smem + L::SUM_OFFSET);
+      // 1. warp w sums rows r_begin + w, + 4, ...: lane l holds vector l of the row
+      for (int r = r_begin + (warp - 2); r < r_end; r += 4 * ROWS_IN_FLIGHT) {
+        uint4 v[ROWS_IN_FLIGHT][MAX_SPLITS];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const uint32_t off = static_cast<uint32_t>(red_vec_index<L::N_MMA / 4>(trow, c / 4 + q)) * 16u;
-            const uint4 v = ld_dsmem_v4(mapa_shared(tile_base + off, static_cast<uint32_t>(sl)));
-            const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+        for (int i = 0; i < ROWS_IN_FLIGHT; ++i) {
+          const int ri = r + 4 * i;
+          const uint32_t off = static_cast<uint32_t>(red_vec_index<VECS>(ri, lane)) * 16u;
 #pragma unroll
-            for (int j = 0; j < 4; ++j) sum[0][4 * q + j] = sl == 0 ? w[j] : Epi::add_partial(sum[0][4 * q + j], w[j]);
-          }
+          for (int sl = 0; sl < MAX_SPLITS; ++sl)
+            if (ri < r_end && sl < k_splits) v[i][sl] = ld_dsmem_v4(mapa_shared(tile_base + off, static_cast<uint32_t>(sl)));
         }
-        Epi{}(epf, est, sum, row, wk.n_blk * BLOCK_N + c, M, N, 0);
+#pragma unroll
+        for (int i = 0; i < ROWS_IN_FLIGHT; ++i) {
+          const int ri = r + 4 * i;
+          if (ri >= r_end) break;
+          uint4 t = v[i][0];
+#pragma unroll
+          for (int sl = 1; sl < MAX_SPLITS; ++sl) {
+            if (sl < k_splits) {
+              t.x = Epi::add_partial(t.x, v[i][sl].x);
+              t.y = Epi::add_partial(t.y, v[i][sl].y);
+              t.z = Epi::add_partial(t.z, v[i][sl].z);
+              t.w = Epi::add_partial(t.w, v[i][sl].w);
+            }
+          }
+          sum_tile[red_vec_index<VECS>(ri - r_begin, lane)] = t;
+        }
+      }
+      epilogue_warps_sync();
+      // 2. the epilogue on 16-column units of the summed rows
+      const int units = (r_end - r_begin) * CHUNKS;
+      for (int u = threadIdx.x - 64; u < units; u += 128) {
+        const int lr = u / CHUNKS, c = (u % CHUNKS) * 16;
+        uint32_t sum[1][16];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 t = sum_tile[red_vec_index<VECS>(lr, c / 4 + q)];
+          sum[0][4 * q] = t.x;
+          sum[0][4 * q + 1] = t.y;
+          sum[0][4 * q + 2] = t.z;
+          sum[0][4 * q + 3] = t.w;
+        }
+        Epi{}(epf, est, sum, row0 + r_begin + lr, wk.n_blk * BLOCK_N + c, M, N, 0);
       }
     }
     cluster_sync();  // no CTA leaves while the others may still read its tile
