@@ -90,12 +90,12 @@ bool pair_mma_enabled() {
   return on;
 }
 
-int gemm_resident_units(const void* kernel, size_t smem, int cg) {
+int gemm_resident_units(const void* kernel, int threads, size_t smem, int cg) {
   int dev = 0;
   cudaGetDevice(&dev);
   static std::mutex mu;
-  static std::map<std::tuple<const void*, size_t, int, int>, int> cache;
-  const auto key = std::make_tuple(kernel, smem, cg, dev);
+  static std::map<std::tuple<const void*, int, size_t, int, int>, int> cache;
+  const auto key = std::make_tuple(kernel, threads, smem, cg, dev);
   std::lock_guard<std::mutex> lk(mu);
   auto it = cache.find(key);
   if (it != cache.end()) return it->second;
@@ -104,12 +104,12 @@ int gemm_resident_units(const void* kernel, size_t smem, int cg) {
   int units = 0;
   if (cg == 1) {
     int occ = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, 192, smem) != cudaSuccess) return 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem) != cudaSuccess) return 0;
     units = occ * num_sms();
   } else {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * num_sms());
-    cfg.blockDim = dim3(192);
+    cfg.blockDim = dim3(static_cast<unsigned>(threads));
     cfg.dynamicSmemBytes = smem;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -26,24 +26,24 @@ int cached_occupancy(const void* kernel, int block, size_t smem);
 // Raises the kernel's dynamic shared-memory limit to at least `smem` bytes on
 // the current device; the attribute call is made once per (kernel, device, size).
 cudaError_t ensure_smem_attr(const void* kernel, size_t smem);
-// For a persistent GEMM kernel (192 threads, `smem` bytes of dynamic shared
-// memory, raised on first use): how many work units can be resident at once
-// on the current device, a unit being one CTA (cg == 1) or one cluster of two
-// CTAs (cg == 2). Cached per (kernel, smem, cg, device); 0 on error.
-int gemm_resident_units(const void* kernel, size_t smem, int cg);
+// For a persistent GEMM kernel (`threads` threads, `smem` bytes of dynamic
+// shared memory, raised on first use): how many work units can be resident at
+// once on the current device, a unit being one CTA (cg == 1) or one cluster of
+// two CTAs (cg == 2). Cached per (kernel, smem, cg, device); 0 on error.
+int gemm_resident_units(const void* kernel, int threads, size_t smem, int cg);
 
 // Two-CTA (cta_group::2) GEMM tiles are used where they apply unless the
 // environment sets TFO_B200_PAIR_MMA=0 (read once per process).
 bool pair_mma_enabled();
 
-// Launches a GEMM kernel (192 threads) on `grid` CTAs as clusters of
+// Launches a GEMM kernel (`threads` threads) on `grid` CTAs as clusters of
 // `cluster` consecutive CTAs (1 = no cluster).
 template <typename... KArgs, typename... Args>
-cudaError_t launch_gemm_grid(void (*kernel)(KArgs...), int grid, int cluster, size_t smem, cudaStream_t st,
-                             Args&&... args) {
+cudaError_t launch_gemm_grid(void (*kernel)(KArgs...), int threads, int grid, int cluster, size_t smem,
+                             cudaStream_t st, Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(192);
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
@@ -64,12 +64,12 @@ cudaError_t launch_gemm_grid(void (*kernel)(KArgs...), int grid, int cluster, si
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
-// Launches a persistent GEMM kernel: `units` work units (see above) of 192
-// threads, as clusters of two CTAs when cg == 2.
+// Launches a persistent GEMM kernel: `units` work units (see above) of
+// `threads` threads, as clusters of two CTAs when cg == 2.
 template <typename... KArgs, typename... Args>
-cudaError_t launch_gemm_units(void (*kernel)(KArgs...), int cg, int units, size_t smem, cudaStream_t st,
-                              Args&&... args) {
-  return launch_gemm_grid(kernel, units * cg, cg, smem, st, std::forward<Args>(args)...);
+cudaError_t launch_gemm_units(void (*kernel)(KArgs...), int threads, int cg, int units, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+  return launch_gemm_grid(kernel, threads, units * cg, cg, smem, st, std::forward<Args>(args)...);
 }
 
 struct RmsNormRopeArgs {

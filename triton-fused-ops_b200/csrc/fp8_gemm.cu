@@ -341,6 +341,8 @@ constexpr int kStages128 = 7;   // 32 KB stages (one CTA per MMA, 128-column til
 constexpr int kStagesPair = 6;  // 32 KB stages (two CTAs per MMA)
 constexpr int stages_for(int bn, int cg) { return cg == 2 ? kStagesPair : (bn == 256 ? kStages : kStages128); }
 constexpr int kGroupM = 16;
+constexpr int kEpiWarps = 8;  // two epilogue warps per TMEM sub-partition
+constexpr int kThreads = gemm_threads(kEpiWarps);
 
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -432,8 +434,8 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
   using L = GemmLayout<BN, 1, STAGES, CG>;
   constexpr bool INT_ACC = (KIND == MmaKind::I8);
   using Epi = Fp8Epi<TO, INT_ACC>;
-  auto kern = umma_gemm_kernel<KIND, BN, 1, STAGES, Epi, B_MN, CG>;
-  const int resident = gemm_resident_units(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, CG);
+  auto kern = umma_gemm_kernel<KIND, BN, 1, STAGES, Epi, B_MN, CG, false, kEpiWarps>;
+  const int resident = gemm_resident_units(reinterpret_cast<const void*>(kern), kThreads, L::SMEM_BYTES, CG);
   if (resident <= 0) return cudaErrorInvalidConfiguration;
   const double codec_k = INT_ACC ? (448.0 / 127.0) * (448.0 / 127.0) : 1.0;
   typename Epi::Params ep{static_cast<TO*>(g.c), g.sa, g.sb, codec_k, g.N,
@@ -445,12 +447,12 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
       // one CTA per (tile, K slice); the slices of a tile form one cluster and
       // sum their raw tiles through distributed shared memory
       using LK = GemmLayout<BN, 1, STAGES, 1, true>;
-      auto kk = umma_gemm_kernel<KIND, BN, 1, STAGES, Epi, B_MN, 1, true>;
-      if (gemm_resident_units(reinterpret_cast<const void*>(kk), LK::SMEM_BYTES, 1) <= 0)
+      auto kk = umma_gemm_kernel<KIND, BN, 1, STAGES, Epi, B_MN, 1, true, kEpiWarps>;
+      if (gemm_resident_units(reinterpret_cast<const void*>(kk), kThreads, LK::SMEM_BYTES, 1) <= 0)
         return cudaErrorInvalidConfiguration;
       typename Epi::Params epk = ep;
       epk.partial = nullptr;
-      cudaError_t ek = launch_gemm_grid(kk, static_cast<int>(work), p.splits, LK::SMEM_BYTES, st, ta, tb, tb,
+      cudaError_t ek = launch_gemm_grid(kk, kThreads, static_cast<int>(work), p.splits, LK::SMEM_BYTES, st, ta, tb, tb,
                                         static_cast<int>(g.M), static_cast<int>(g.N), static_cast<int>(p.Kp),
                                         kGroupM, idesc, epk, error_word_ptr(), p.splits);
       note_launch();
@@ -458,7 +460,7 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
     }
   }
   const int units = static_cast<int>(std::min<int64_t>(work, resident));
-  cudaError_t e = launch_gemm_units(kern, CG, units, L::SMEM_BYTES, st, ta, tb, tb, static_cast<int>(g.M),
+  cudaError_t e = launch_gemm_units(kern, kThreads, CG, units, L::SMEM_BYTES, st, ta, tb, tb, static_cast<int>(g.M),
                                     static_cast<int>(g.N), static_cast<int>(p.Kp), kGroupM, idesc, ep,
                                     error_word_ptr(), p.splits);
   note_launch();

@@ -198,14 +198,14 @@ cudaError_t launch_umma_cg(const CUtensorMap& tx, const CUtensorMap& tg, const C
   using L = GemmLayout<kBlockN, 2, STAGES, CG>;
   using Epi = GatedEpi<TO, ACT>;
   auto kern = umma_gemm_kernel<KIND, kBlockN, 2, STAGES, Epi, false, CG>;
-  const int resident = gemm_resident_units(reinterpret_cast<const void*>(kern), L::SMEM_BYTES, CG);
+  const int resident = gemm_resident_units(reinterpret_cast<const void*>(kern), gemm_threads(4), L::SMEM_BYTES, CG);
   if (resident <= 0) return cudaErrorInvalidConfiguration;
   typename Epi::Params ep{static_cast<TO*>(g.out), g.N, al16(g.out) && (g.N * sizeof(TO)) % 16 == 0, g.codes,
                           g.scale, g.e4m3, g.amax_parts};
   const int64_t tiles = ((g.M + L::PAIR_M - 1) / L::PAIR_M) * ((g.N + kBlockN - 1) / kBlockN);
   const int units = static_cast<int>(std::min<int64_t>(tiles, resident));
   if (g.ctas_out != nullptr) *g.ctas_out = units * CG;
-  cudaError_t e = launch_gemm_units(kern, CG, units, L::SMEM_BYTES, st, tx, tg, tu, static_cast<int>(g.M),
+  cudaError_t e = launch_gemm_units(kern, gemm_threads(4), CG, units, L::SMEM_BYTES, st, tx, tg, tu, static_cast<int>(g.M),
                                     static_cast<int>(g.N), static_cast<int>(g.K), kGroupM, idesc, ep,
                                     error_word_ptr(), 1);
   note_launch();

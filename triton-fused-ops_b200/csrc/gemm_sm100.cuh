@@ -11,8 +11,12 @@
 // tile's mainloop runs. NUM_B = 2 shares every A tile between two B operands
 // (the gate and up projections of the gated MLP).
 //
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = MMA issuer and
-// TMEM owner, warps 2-5 = epilogue (warp w reads TMEM lanes 32*(w%4)..+31).
+// Warp roles (64 + 32 * EPI_WARPS threads): warp 0 = TMA producer, warp 1 =
+// MMA issuer and TMEM owner, warps 2.. = epilogue. Epilogue warp w reads TMEM
+// lanes 32*(w%4)..+31 (the lanes its sub-partition may access); with 8
+// epilogue warps two warps share those lanes and each drains half of the
+// tile's columns, so that every scheduler has two epilogue warps to
+// interleave (one warp alone leaves every instruction latency exposed).
 //
 // Every mbarrier wait is bounded; a wait that runs out of budget records a
 // bit in the device error word, raises a CTA-wide abort flag that the other
@@ -97,8 +101,13 @@ __device__ __forceinline__ uint4 ld_dsmem_v4(uint32_t cluster_addr) {
   return r;
 }
 
-// Barrier 1 over the four epilogue warps (barrier 0 is __syncthreads).
-__device__ __forceinline__ void epilogue_warps_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier 1 over the epilogue warps (barrier 0 is __syncthreads).
+__device__ __forceinline__ void epilogue_warps_sync(int threads) {
+  asm volatile("bar.sync 1, %0;" ::"r"(threads) : "memory");
+}
+
+// Threads of a GEMM kernel with EPI_WARPS epilogue warps.
+constexpr int gemm_threads(int epi_warps) { return 64 + 32 * epi_warps; }
 
 // Waits for `parity` on `bar`, giving up when the CTA abort flag is raised or
 // the budget runs out (then sets the error bit and raises the flag).
@@ -155,8 +164,8 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 // must provide add_partial and final_params). A second cluster barrier keeps
 // every tile readable until all CTAs are done. 2 <= k_splits <= 8.
 template <MmaKind KIND, int BLOCK_N, int NUM_B, int STAGES, class Epi, bool B_MN = false, int CG = 1,
-          bool KSPLIT = false>
-__global__ void __launch_bounds__(192, 1)
+          bool KSPLIT = false, int EPI_WARPS = 4>
+__global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
                      const __grid_constant__ CUtensorMap tmap_b1, int M, int N, int K, int group_m, uint32_t idesc,
                      const typename Epi::Params ep, uint32_t* err, int k_splits) {
@@ -214,7 +223,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4 * CG);
+      mbar_init(&tempty[b], EPI_WARPS * CG);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -343,7 +352,11 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     // ------------------------------------------------------------ epilogue
+    static_assert(EPI_WARPS == 4 || EPI_WARPS == 8, "one or two epilogue warps per TMEM sub-partition");
+    constexpr int COLS = BLOCK_N / (EPI_WARPS / 4);  // columns per epilogue warp (per B operand)
+    static_assert(COLS % 32 == 0, "epilogue walks 32 columns per iteration");
     const int sub = warp & 3;
+    const int col_lo = ((warp - 2) >> 2) * COLS;  // this warp's first column of the tile
     const int row_in_tile = static_cast<int>(rank) * L::BM + sub * 32 + lane;
     const uint32_t lane_addr = static_cast<uint32_t>(sub * 32) << 16;
     est = Epi::init(ep);
@@ -371,10 +384,11 @@ __global__ void __launch_bounds__(192, 1)
         // raw accumulators to the reduction tile (row = this thread's TMEM lane)
         const int trow = sub * 32 + lane;
 #pragma unroll 1
-        for (int c = 0; c < BLOCK_N; c += 16) {
+        for (int c = col_lo; c < col_lo + COLS; c += 16) {
           uint32_t r[16];
           tmem_ld16(base + c, r);
           tmem_ld_wait();
+          tmem_ld_fence(r);
 #pragma unroll
           for (int q = 0; q < 4; ++q)
             red_tile[red_vec_index<L::N_MMA / 4>(trow, c / 4 + q)] =
@@ -385,23 +399,28 @@ __global__ void __launch_bounds__(192, 1)
         if (lane == 0) mbar_arrive(&tempty[acc]);
         continue;
       }
-      static_assert(BLOCK_N % 32 == 0, "epilogue walks 32 columns per iteration");
       uint32_t ra[NUM_B][16], rb[NUM_B][16];
 #pragma unroll
-      for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N, ra[j]);
+      for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N + col_lo, ra[j]);
       tmem_ld_wait();
+#pragma unroll
+      for (int j = 0; j < NUM_B; ++j) tmem_ld_fence(ra[j]);
 #pragma unroll 1
-      for (int c = 0; c < BLOCK_N; c += 32) {
+      for (int c = col_lo; c < col_lo + COLS; c += 32) {
 #pragma unroll
         for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N + c + 16, rb[j]);
         Epi{}(ep, est, ra, row, wk.n_blk * BLOCK_N + c, M, N, wk.split);
         tmem_ld_wait();
-        if (c + 32 < BLOCK_N) {
+#pragma unroll
+        for (int j = 0; j < NUM_B; ++j) tmem_ld_fence(rb[j]);
+        if (c + 32 < col_lo + COLS) {
 #pragma unroll
           for (int j = 0; j < NUM_B; ++j) tmem_ld16(base + j * BLOCK_N + c + 32, ra[j]);
         }
         Epi{}(ep, est, rb, row, wk.n_blk * BLOCK_N + c + 16, M, N, wk.split);
         tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < NUM_B; ++j) tmem_ld_fence(ra[j]);
       }
       tc_fence_before();
       __syncwarp();
@@ -431,12 +450,12 @@ __global__ void __launch_bounds__(192, 1)
       const int r_end = min(rows, r_begin + per);
       const uint32_t tile_base = smem_u32(red_tile);
       uint4* sum_tile = reinterpret_cast<uint4*>(smem + L::SUM_OFFSET);
-      // 1. warp w sums rows r_begin + w, + 4, ...: lane l holds vector l of the row
-      for (int r = r_begin + (warp - 2); r < r_end; r += 4 * ROWS_IN_FLIGHT) {
+      // 1. epilogue warp w sums rows r_begin + w, + EPI_WARPS, ...: lane l holds vector l of the row
+      for (int r = r_begin + (warp - 2); r < r_end; r += EPI_WARPS * ROWS_IN_FLIGHT) {
         uint4 v[ROWS_IN_FLIGHT][MAX_SPLITS];
 #pragma unroll
         for (int i = 0; i < ROWS_IN_FLIGHT; ++i) {
-          const int ri = r + 4 * i;
+          const int ri = r + EPI_WARPS * i;
           const uint32_t off = static_cast<uint32_t>(red_vec_index<VECS>(ri, lane)) * 16u;
 #pragma unroll
           for (int sl = 0; sl < MAX_SPLITS; ++sl)
@@ -444,7 +463,7 @@ __global__ void __launch_bounds__(192, 1)
         }
 #pragma unroll
         for (int i = 0; i < ROWS_IN_FLIGHT; ++i) {
-          const int ri = r + 4 * i;
+          const int ri = r + EPI_WARPS * i;
           if (ri >= r_end) break;
           uint4 t = v[i][0];
 #pragma unroll
@@ -459,10 +478,10 @@ __global__ void __launch_bounds__(192, 1)
           sum_tile[red_vec_index<VECS>(ri - r_begin, lane)] = t;
         }
       }
-      epilogue_warps_sync();
+      epilogue_warps_sync(32 * EPI_WARPS);
       // 2. the epilogue on 16-column units of the summed rows
       const int units = (r_end - r_begin) * CHUNKS;
-      for (int u = threadIdx.x - 64; u < units; u += 128) {
+      for (int u = threadIdx.x - 64; u < units; u += 32 * EPI_WARPS) {
         const int lr = u / CHUNKS, c = (u % CHUNKS) * 16;
         uint32_t sum[1][16];
 #pragma unroll
