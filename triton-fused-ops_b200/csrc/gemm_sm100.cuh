@@ -6,7 +6,7 @@
 // A and every B_j are K-major (rows of K), staged by TMA into a STAGES-deep
 // shared-memory ring with the 128-byte swizzle; one elected thread issues
 // tcgen05.mma (M = 128, N = BLOCK_N, 32 bytes of K per instruction) into a
-// double-buffered TMEM accumulator (2 x NUM_B x BLOCK_N columns), and four
+// double-buffered TMEM accumulator (2 x NUM_B x BLOCK_N columns), and the
 // epilogue warps drain the finished buffer with tcgen05.ld while the next
 // tile's mainloop runs. NUM_B = 2 shares every A tile between two B operands
 // (the gate and up projections of the gated MLP).
@@ -134,7 +134,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 //                              int M, int N, int split)
 //   called once per 16 accumulator columns per row (row < M not guaranteed);
 //   static __device__ void finish(const Params&, State&)
-//   called by every epilogue thread (4 full warps) after its last tile.
+//   called by every epilogue thread (EPI_WARPS full warps) after its last tile.
 //
 // B_MN: the B operand is MN-major (B given as [K, N] with N contiguous, as
 // the reference's fp8_gemm passes it); each stage then holds B_ROWS / 128
@@ -203,8 +203,9 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     const int tile = w / k_splits;
     r.split = w - tile * k_splits;
     sched.coords(tile, r.m_blk, r.n_blk);
-    r.kb0 = static_cast<int>(static_cast<int64_t>(r.split) * num_k / k_splits);
-    r.kb1 = static_cast<int>(static_cast<int64_t>(r.split + 1) * num_k / k_splits);
+    // floor(split * num_k / k_splits) in 32-bit arithmetic without the product
+    r.kb0 = r.split * (num_k / k_splits) + (r.split * (num_k % k_splits)) / k_splits;
+    r.kb1 = (r.split + 1) * (num_k / k_splits) + ((r.split + 1) * (num_k % k_splits)) / k_splits;
     return r;
   };
   uint4* red_tile = reinterpret_cast<uint4*>(smem);
