@@ -427,6 +427,12 @@ def components(peaks, flush_buf):
     cq, sq = rope_tables(8192, 64, dev)
     rows = 8 * 8192
     two = torch.tensor(2.0, device=dev)
+    # RMSNorm+RoPE alone at the same shape, two alternating 512 MB inputs (each
+    # call starts with its input out of L2): the kernel's own HBM rate. The
+    # step's roofline_rmsnorm_rope figure also pays for writing the previous
+    # step's gated-MLP output back from L2 while the kernel runs.
+    us, err = time_graph([lambda x=x: triton_ops.fused_rmsnorm_rope(x, wq, cq, sq) for x in xq], reps=5)
+    out["rmsnorm_rope_8x8192x4096"] = entry(us, err, None, nbytes=rows * RMS_BYTES_PER_ROW + 4096 * 2 + 2 * 8192 * 32 * 2)
     fq = {}
     us, err = time_graph([lambda x=x: triton_ops.fused_rmsnorm_rope_quantize(x, wq, cq, sq) for x in xq], reps=5)
     fq["dynamic_scale"] = entry(us, err, None, nbytes=rows * (8192 + 4096))
