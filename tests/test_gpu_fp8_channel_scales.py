@@ -1,4 +1,4 @@
-"""Per-token / per-channel FP8 scales (SURVEY next-step: scale vectors in the GEMM epilogue).
+"""Per-token / per-channel FP8 scales: scale vectors applied in the GEMM epilogue.
 
 The reference's FP8Format.compute_scale_per_channel (models.py:301-314) is a
 torch expression; its quantize/dequantize kernels read one scale. Here the
