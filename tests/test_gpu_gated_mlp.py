@@ -77,7 +77,7 @@ def test_shapes_dtypes_paths(cuda, M, N, K, xd, wd, act):
 
 
 def test_weights_swapped_gives_activation_on_gate(cuda):
-    """The BASELINE form act(x Wg^T) * (x Wu^T) is the reference op with the weights swapped."""
+    """The textbook form act(x Wg^T) * (x Wu^T) is the reference op with the two weights swapped."""
     from triton_ops import fused_gated_mlp
 
     x, wg, wu = mlp_inputs(256, 512, 512, seed=9)
