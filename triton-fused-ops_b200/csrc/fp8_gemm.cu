@@ -81,6 +81,7 @@ __global__ void __launch_bounds__(256) prep_transpose_kernel(const uint8_t* __re
 // Sign flip + sums for the single-operand staging of the reference codec.
 // Rows: dst[r, :] = src[r, :] ^ 0x80 (as int8) and sums[r] = sum of the
 // row's int8 values; one warp per row, K % 16 == 0, 16-byte aligned rows.
+constexpr int kRowUnroll = 8;
 __global__ void __launch_bounds__(256) prep_rows_s8_sum_kernel(const uint8_t* __restrict__ src, int64_t R, int64_t K,
                                                                int8_t* __restrict__ dst, int32_t* __restrict__ sums) {
   const int lane = threadIdx.x & 31;
@@ -89,14 +90,26 @@ __global__ void __launch_bounds__(256) prep_rows_s8_sum_kernel(const uint8_t* __
     const uint4* s4 = reinterpret_cast<const uint4*>(src + r * K);
     uint4* d4 = reinterpret_cast<uint4*>(dst + r * K);
     int acc = 0;
-    for (int64_t c = lane; c < K / 16; c += 32) {
-      uint4 u = __ldcs(s4 + c);
-      u.x ^= 0x80808080u; u.y ^= 0x80808080u; u.z ^= 0x80808080u; u.w ^= 0x80808080u;
-      acc = __dp4a(static_cast<int>(u.x), 0x01010101, acc);
-      acc = __dp4a(static_cast<int>(u.y), 0x01010101, acc);
-      acc = __dp4a(static_cast<int>(u.z), 0x01010101, acc);
-      acc = __dp4a(static_cast<int>(u.w), 0x01010101, acc);
-      d4[c] = u;
+    // kRowUnroll 16-byte loads per lane are issued before the first is used:
+    // a 4 KB row is one DRAM round trip, not eight in sequence
+    const int64_t nv = K / 16;
+    for (int64_t c0 = lane; c0 < nv; c0 += 32 * kRowUnroll) {
+      uint4 u[kRowUnroll];
+#pragma unroll
+      for (int i = 0; i < kRowUnroll; ++i)
+        if (c0 + 32 * i < nv) u[i] = __ldcs(s4 + c0 + 32 * i);
+#pragma unroll
+      for (int i = 0; i < kRowUnroll; ++i) {
+        if (c0 + 32 * i < nv) {
+          uint4 v = u[i];
+          v.x ^= 0x80808080u; v.y ^= 0x80808080u; v.z ^= 0x80808080u; v.w ^= 0x80808080u;
+          acc = __dp4a(static_cast<int>(v.x), 0x01010101, acc);
+          acc = __dp4a(static_cast<int>(v.y), 0x01010101, acc);
+          acc = __dp4a(static_cast<int>(v.z), 0x01010101, acc);
+          acc = __dp4a(static_cast<int>(v.w), 0x01010101, acc);
+          d4[c0 + 32 * i] = v;
+        }
+      }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
