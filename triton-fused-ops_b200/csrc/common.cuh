@@ -399,6 +399,12 @@ __device__ __forceinline__ F2 fma2(F2 a, F2 b, F2 c) {
 // kernel has completed and its memory is visible (a no-op otherwise).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel in the stream, when launched as a programmatic
+// dependent, be scheduled now (on SMs this grid leaves free) and run its
+// pre-wait setup; it still sees this grid's memory only after griddep_wait().
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 
 // ---------------------------------------------------------------------------
 // misc

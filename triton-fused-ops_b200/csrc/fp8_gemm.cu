@@ -27,6 +27,7 @@ namespace tfo {
 // dst[r, k] = k < K ? src[r * lds + k] ^ flip : 0, for k < Kp (Kp % 16 == 0).
 __global__ void prep_rows_kernel(const uint8_t* __restrict__ src, int64_t R, int64_t K, int64_t lds,
                                  uint8_t* __restrict__ dst, int64_t Kp, uint32_t flip, bool vec_src) {
+  griddep_launch_dependents();  // the GEMM that follows may set up meanwhile
   const int64_t chunks_per_row = Kp / 16;
   const int64_t total = R * chunks_per_row;
   const uint32_t f4 = flip * 0x01010101u;
@@ -54,6 +55,7 @@ __global__ void prep_rows_kernel(const uint8_t* __restrict__ src, int64_t R, int
 // dst[n, k] = k < K ? src[k * N + n] ^ flip : 0 (dst is [N, Kp]); 64 x 64 tiles.
 __global__ void __launch_bounds__(256) prep_transpose_kernel(const uint8_t* __restrict__ src, int64_t K, int64_t N,
                                                              uint8_t* __restrict__ dst, int64_t Kp, uint32_t flip) {
+  griddep_launch_dependents();  // the GEMM that follows may set up meanwhile
   __shared__ uint8_t tile[64][68];
   const int64_t k0 = static_cast<int64_t>(blockIdx.y) * 64;
   const int64_t n0 = static_cast<int64_t>(blockIdx.x) * 64;
@@ -84,6 +86,7 @@ __global__ void __launch_bounds__(256) prep_transpose_kernel(const uint8_t* __re
 constexpr int kRowUnroll = 8;
 __global__ void __launch_bounds__(256) prep_rows_s8_sum_kernel(const uint8_t* __restrict__ src, int64_t R, int64_t K,
                                                                int8_t* __restrict__ dst, int32_t* __restrict__ sums) {
+  griddep_launch_dependents();  // the GEMM that follows may set up meanwhile
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < R; r += warps) {
@@ -133,6 +136,7 @@ static_assert(kColRows * 255 < 65536 && kColRows % kColUnroll == 0, "16-bit lane
 __global__ void __launch_bounds__(kColThreads) prep_cols_s8_sum_kernel(const uint8_t* __restrict__ src, int64_t K,
                                                                         int64_t N, int8_t* __restrict__ dst,
                                                                         int32_t* __restrict__ sums) {
+  griddep_launch_dependents();  // the GEMM that follows may set up meanwhile
   __shared__ int32_t part[kColGroups][kColChunks * 17];  // 17-word stride: no bank conflicts
   const int cx = threadIdx.x % kColChunks, g = threadIdx.x / kColChunks;
   const int64_t chunks = N / 16;
@@ -304,6 +308,7 @@ struct Fp8Epi {
 __global__ void fp8_scale_vectors_kernel(const float* __restrict__ sa, const float* __restrict__ sa_rows,
                                          const float* __restrict__ sb, const float* __restrict__ sb_cols, int64_t M,
                                          int64_t N, double codec_k, float* __restrict__ ra, float* __restrict__ rb) {
+  griddep_launch_dependents();  // the GEMM that follows may set up meanwhile
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < M + N;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
     if (i < M) ra[i] = static_cast<float>(codec_k / static_cast<double>(sa_rows != nullptr ? sa_rows[i] : *sa));
