@@ -174,6 +174,7 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const T* __restrict
                                                              const float* __restrict__ scale_in,
                                                              const uint32_t* __restrict__ partials, int nparts,
                                                              float* __restrict__ scale_out, uint8_t* __restrict__ out) {
+  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
   __shared__ float s_sh;
   __shared__ uint32_t red[32];
   if (partials != nullptr) {
@@ -246,6 +247,7 @@ __global__ void __launch_bounds__(kQuantThreads, 2)
     quantize_dynamic_kernel(const T* __restrict__ x, int64_t n, bool vec, uint32_t* __restrict__ barrier,
                             float* __restrict__ scale_out,
                             uint8_t* __restrict__ out, uint32_t* __restrict__ err) {
+  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
   __shared__ uint32_t red[32];
   __shared__ float s_sh;
   __shared__ int ok_sh;
@@ -276,6 +278,7 @@ __global__ void __launch_bounds__(kResThreads, 1)
     quantize_resident_kernel(const T* __restrict__ x, int64_t n, int64_t vecs_per_cta, uint32_t* __restrict__ barrier,
                              float* __restrict__ scale_out,
                              uint8_t* __restrict__ out, uint32_t* __restrict__ err) {
+  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
   constexpr int EV = 16 / sizeof(T);  // elements per 16-byte vector
   extern __shared__ __align__(128) uint4 slab[];
   __shared__ uint64_t bars[kResPieces];
@@ -398,6 +401,7 @@ template <typename T, bool E4M3>
 __global__ void __launch_bounds__(kRowThreads) encode_rows_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
                                                                   const float* __restrict__ scales,
                                                                   uint8_t* __restrict__ out) {
+  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
   const int64_t n = rows * cols;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x; i < n;
        i += static_cast<int64_t>(gridDim.x) * kRowThreads) {

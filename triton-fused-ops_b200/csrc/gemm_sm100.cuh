@@ -169,6 +169,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
                      const __grid_constant__ CUtensorMap tmap_b1, int M, int N, int K, int group_m, uint32_t idesc,
                      const typename Epi::Params ep, uint32_t* err, int k_splits) {
+  griddep_launch_dependents();  // a programmatic-dependent GEMM after this one may be scheduled as CTAs retire
   static_assert(!B_MN || (NUM_B == 1 && KindTraits<KIND>::ELEM == 1 && BLOCK_N % 128 == 0),
                 "MN-major B: 8-bit operands, one B operand, BLOCK_N a multiple of 128");
   using L = GemmLayout<BLOCK_N, NUM_B, STAGES, CG, KSPLIT>;

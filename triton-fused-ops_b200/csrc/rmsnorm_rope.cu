@@ -122,6 +122,7 @@ __global__ void __launch_bounds__(256, 4) rmsnorm_rope_vec_kernel(
     const TX* __restrict__ x, const void* __restrict__ w, const TCS* __restrict__ cosp, const TCS* __restrict__ sinp,
     TX* __restrict__ out, int64_t rows, int seq_len, int hidden, int head_dim, int rot_cols, int64_t cs_ss,
     int64_t cs_sd, float eps, int w_dtype, int stages, uint32_t* err) {
+  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
   constexpr int E = Pack<TX>::E;
   // With 16-bit x and tables, y*c and p*s are exact in fp32, so the
   // reference's RN(RN(y*c) -/+ RN(p*s)) equals one FMA on an exact product.
@@ -324,6 +325,7 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
     const TX* __restrict__ x, const void* __restrict__ w, const TCS* __restrict__ cosp, const TCS* __restrict__ sinp,
     TX* __restrict__ out, int64_t rows, int seq_len, int hidden, int head_dim, int rot_cols, int64_t cs_ss,
     int64_t cs_sd, float eps, int w_dtype, int cs_stride, uint32_t* err, const RowQuantArgs q) {
+  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
   constexpr int E = Pack<TX>::E;
   constexpr bool kExactProducts = sizeof(TX) == 2 && sizeof(TCS) == 2;
   const int W = blockDim.x >> 5;
@@ -491,6 +493,7 @@ __global__ void __launch_bounds__(256) rmsnorm_rope_generic_kernel(
     const TX* __restrict__ x, const void* __restrict__ w, const void* __restrict__ cosp, const void* __restrict__ sinp,
     TX* __restrict__ out, int64_t rows, int seq_len, int hidden, int head_dim, int rot_cols, int64_t cs_ss,
     int64_t cs_sd, float eps, int w_dtype, int cos_dtype, int sin_dtype) {
+  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
   extern __shared__ float rowbuf[];
   __shared__ float red[32];
   const int t = threadIdx.x, T = blockDim.x;
