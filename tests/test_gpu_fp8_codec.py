@@ -248,3 +248,50 @@ def test_dynamic_scale_nan_and_inf_inputs(cuda):
         s_ref = O.compute_scale(x)
         assert f32bits(s.item()) == f32bits(s_ref)
         np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(x, s_ref))
+
+
+@pytest.mark.parametrize("dtype", ["f16", "bf16", "f32"])
+@pytest.mark.parametrize("nvec", [1, 1023, 1024, 1025, 8193, 65535, 65536, 65537])
+def test_dynamic_scale_one_cluster_form(cuda, dtype, nvec):
+    """Aligned tensors of up to 65536 16-byte vectors take the one-cluster form (one launch, no
+    barrier memset; 1-8 CTAs, 2-16 vectors per thread); larger ones the grid-barrier forms. Same
+    bytes either way."""
+    import torch as _t
+
+    from triton_ops import _lib, quantize_fp8
+
+    ev = 16 // (4 if dtype == "f32" else 2)
+    n = nvec * ev
+    rng = np.random.default_rng(nvec)
+    x = O.round_to((rng.standard_normal(n) * 3).astype(np.float32), dtype)
+    xt = dev_tensor(x, dtype)
+    for code in (_t.uint8, _t.float8_e4m3fn):
+        n0 = _lib.kernel_launches()
+        q, s = quantize_fp8(xt, dtype=code)
+        launches = _lib.kernel_launches() - n0
+        assert (launches == 1) == (nvec <= 65536), launches
+        s_ref = O.compute_scale(x)
+        assert f32bits(s.item()) == f32bits(s_ref)
+        if code == _t.uint8:
+            np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(x, s_ref))
+        else:
+            ref = (_t.from_numpy(x.astype(np.float32)) * _t.tensor(s_ref)).clamp(-448, 448).to(_t.float8_e4m3fn)
+            assert _t.equal(q.view(_t.uint8).cpu(), ref.view(_t.uint8))
+    assert _lib.device_error_flags() == 0
+
+
+def test_one_cluster_form_nan_inf_and_zero(cuda):
+    """The one-cluster form's NaN / inf / all-zero scales and codes equal the oracle's."""
+    from triton_ops import quantize_fp8
+
+    rng = np.random.default_rng(4)
+    for bad in (np.nan, np.inf, -np.inf, 0.0):
+        x = rng.standard_normal(4096).astype(np.float32)
+        if bad == 0.0:
+            x[:] = 0.0
+        else:
+            x[17] = bad
+        q, s = quantize_fp8(torch.from_numpy(x).cuda())
+        s_ref = O.compute_scale(x)
+        assert f32bits(s.item()) == f32bits(s_ref)
+        np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(x, s_ref))

@@ -52,9 +52,10 @@ def check_equal(B, S, H, D, dt, num_heads=None, scale=None, dtype=torch.uint8, s
     q, s = fused_rmsnorm_rope_quantize(x, w, cos, sin, 1e-6, num_heads, st, dtype=dtype)
     launches = _lib.kernel_launches() - n0
     # dynamic scale: rows + amax partials, then the encode (2 launches) on the
-    # warp-per-row layout; otherwise RMSNorm+RoPE, memset, quantize (3)
+    # warp-per-row layout; otherwise RMSNorm+RoPE, then the quantize (one
+    # launch for small tensors, a barrier memset and a launch for larger ones)
     if scale is None:
-        assert (launches == 2) == fused, launches
+        assert launches == 2 if fused else launches in (2, 3), launches
     q_ref, s_ref = composed(x, w, cos, sin, num_heads, st, dtype)
     assert q.dtype == dtype and q.shape == x.shape
     assert s.item() == s_ref.item() or (np.isnan(s.item()) and np.isnan(s_ref.item()))
