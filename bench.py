@@ -379,6 +379,18 @@ def components(peaks, flush_buf):
         del qs
     del ts
 
+    # decode-size activations: dynamic-scale quantize of [16, 4096] fp16 and
+    # FP8Linear(4096 -> 4096, bias) on it (quantize + codec GEMM + bias epilogue)
+    xd = [torch.randn(1, 16, 4096, device=dev, generator=g).half() for _ in range(16)]
+    us, err = time_graph([lambda x=x: triton_ops.quantize_fp8(x) for x in xd])
+    us_call = 1e3 * time_events(lambda: triton_ops.quantize_fp8(xd[0]), 30, flush_buf)
+    out["fp8_quantize_16x4096"] = entry(us, err, us_call, nbytes=3 * 16 * 4096)
+    lin = triton_ops.FP8Linear(4096, 4096, bias=True).to(dev).half()
+    us, err = time_graph([lambda x=x: lin(x) for x in xd])
+    us_call = 1e3 * time_events(lambda: lin(xd[0]), 30, flush_buf)
+    out["fp8linear_16x4096x4096"] = entry(us, err, us_call, flops=2.0 * 16 * 4096 * 4096)
+    del xd, lin
+
     # FP8 GEMM over M, N = K = 4096: reference codec (int8 tensor cores), e4m3
     # (fp8 tensor cores), and the library fp8 GEMM (torch._scaled_mm) on the
     # same e4m3 operands as a comparator

@@ -64,6 +64,24 @@ cudaError_t launch_gemm_grid(void (*kernel)(KArgs...), int threads, int grid, in
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 
+// Launches an ordinary kernel as a programmatic dependent of the previous
+// kernel on the stream: it may be scheduled while that kernel runs and must
+// execute griddepcontrol.wait before touching global memory.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), int grid, int block, cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(block));
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
 // Launches a persistent GEMM kernel: `units` work units (see above) of
 // `threads` threads, as clusters of two CTAs when cg == 2.
 template <typename... KArgs, typename... Args>

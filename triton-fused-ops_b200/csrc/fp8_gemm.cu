@@ -87,6 +87,7 @@ constexpr int kRowUnroll = 8;
 __global__ void __launch_bounds__(256) prep_rows_s8_sum_kernel(const uint8_t* __restrict__ src, int64_t R, int64_t K,
                                                                int8_t* __restrict__ dst, int32_t* __restrict__ sums) {
   griddep_launch_dependents();  // the GEMM that follows may set up meanwhile
+  griddep_wait();  // launched as a programmatic dependent: inputs are read after this
   const int lane = threadIdx.x & 31;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t r = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); r < R; r += warps) {
@@ -580,8 +581,9 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
     int32_t* sums = reinterpret_cast<int32_t*>(ws + p.off_sum);
     int8_t* da = reinterpret_cast<int8_t*>(ws + p.off_a);
     const int grid = static_cast<int>(std::min<int64_t>((g.M + 7) / 8, num_sms() * 8));
-    prep_rows_s8_sum_kernel<<<grid, 256, 0, st>>>(a, g.M, g.K, da, sums);
+    e = launch_dependent(prep_rows_s8_sum_kernel, grid, 256, st, a, g.M, g.K, da, sums);
     note_launch();
+    if (e != cudaSuccess) return e;
     a = reinterpret_cast<const uint8_t*>(da);
     corr_row = sums;
     b_fmt = 0;  // B stays raw u8
@@ -600,8 +602,9 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
       note_launch();
     } else {
       const int grid = static_cast<int>(std::min<int64_t>((g.N + 7) / 8, num_sms() * 8));
-      prep_rows_s8_sum_kernel<<<grid, 256, 0, st>>>(b, g.N, g.K, db, sums);
+      e = launch_dependent(prep_rows_s8_sum_kernel, grid, 256, st, b, g.N, g.K, db, sums);
       note_launch();
+      if (e != cudaSuccess) return e;
     }
     b = reinterpret_cast<const uint8_t*>(db);
     corr_col = sums;
