@@ -401,6 +401,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
     quantize_small_kernel(const T* __restrict__ x, int64_t nvec, float* __restrict__ scale_out,
                           uint8_t* __restrict__ out) {
   griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
+  griddep_wait();               // launched as a programmatic dependent: x is read after this
   __shared__ uint32_t red[32];
   __shared__ uint32_t cta_max;
   // vector i of this thread: base + i * stride (the cluster's threads in turn)
@@ -731,13 +732,15 @@ cudaError_t quant_small_t(const void* x, int64_t n, float* scale_out, void* out,
   cfg.blockDim = dim3(kSmallThreads);
   cfg.dynamicSmemBytes = 0;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = static_cast<unsigned>(ctas);
   attr[0].val.clusterDim.y = 1;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   cudaError_t e = cudaLaunchKernelEx(&cfg, quantize_small_kernel<T, E4M3>, static_cast<const T*>(x), nvec, scale_out,
                                      static_cast<uint8_t*>(out));
   note_launch();
