@@ -358,7 +358,10 @@ namespace {
 constexpr int kStages = 4;      // 48 KB stages (one CTA per MMA, 256-column tiles)
 constexpr int kStages128 = 7;   // 32 KB stages (one CTA per MMA, 128-column tiles)
 constexpr int kStagesPair = 6;  // 32 KB stages (two CTAs per MMA)
-constexpr int stages_for(int bn, int cg) { return cg == 2 ? kStagesPair : (bn == 256 ? kStages : kStages128); }
+constexpr int kStagesSmallA = 11;  // 20 KB stages (128-column tiles, 32-row A stages for M <= 32)
+constexpr int stages_for(int bn, int cg, int a_rows = 128) {
+  return cg == 2 ? kStagesPair : (bn == 256 ? kStages : (a_rows == 32 ? kStagesSmallA : kStages128));
+}
 constexpr int kGroupM = 16;
 constexpr int kEpiWarps = 8;  // two epilogue warps per TMEM sub-partition
 constexpr int kThreads = gemm_threads(kEpiWarps);
@@ -380,6 +383,7 @@ struct Fp8Plan {
   bool b_mn;            // B read MN-major from [K, N]
   size_t off_a, off_b, off_sum, off_part, off_vec, bytes;
   int bn, cg, splits;
+  int a_rows;           // rows of an A stage: 32 for M <= 32 with 128-column single-CTA tiles, else 128
   bool ksplit_cluster;  // K slices of a tile reduced inside one cluster (no partials, no finalize)
 };
 
@@ -398,6 +402,9 @@ void pick_tiles(int64_t M, int64_t N, int64_t Kp, Fp8Plan& p) {
   p.splits = 1;
   if (tiles < units / 2) p.splits = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(num_k / 4, units / tiles)));
   p.ksplit_cluster = (p.splits > 1 && p.splits <= 8 && p.cg == 1 && p.bn == 128);
+  // few rows: 32-row A stages (4 KB instead of 16 KB of mostly zero-filled
+  // rows), so 11 stages fit and a K slice's blocks are all requested at once
+  p.a_rows = (p.cg == 1 && p.bn == 128 && M <= 32) ? 32 : 128;
 }
 
 Fp8Plan plan_fp8(const Fp8GemmArgs& g, bool assume_aligned) {
@@ -439,7 +446,7 @@ Fp8Plan plan_fp8(const Fp8GemmArgs& g, bool assume_aligned) {
   return p;
 }
 
-template <MmaKind KIND, int BN, typename TO, bool B_MN, int CG>
+template <MmaKind KIND, int BN, typename TO, bool B_MN, int CG, int A_ROWS>
 cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, const Fp8Plan& p,
                             uint32_t idesc, const int32_t* corr_row, const int32_t* corr_col, uint32_t* partial,
                             cudaStream_t st) {
@@ -449,11 +456,11 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
     ra = reinterpret_cast<const float*>(static_cast<uint8_t*>(g.ws) + p.off_vec);
     rb = ra + g.M;
   }
-  constexpr int STAGES = stages_for(BN, CG);
-  using L = GemmLayout<BN, 1, STAGES, CG>;
+  constexpr int STAGES = stages_for(BN, CG, A_ROWS);
+  using L = GemmLayout<BN, 1, STAGES, CG, false, A_ROWS>;
   constexpr bool INT_ACC = (KIND == MmaKind::I8);
   using Epi = Fp8Epi<TO, INT_ACC>;
-  auto kern = umma_gemm_kernel<KIND, BN, 1, STAGES, Epi, B_MN, CG, false, kEpiWarps>;
+  auto kern = umma_gemm_kernel<KIND, BN, 1, STAGES, Epi, B_MN, CG, false, kEpiWarps, A_ROWS>;
   const int resident = gemm_resident_units(reinterpret_cast<const void*>(kern), kThreads, L::SMEM_BYTES, CG);
   if (resident <= 0) return cudaErrorInvalidConfiguration;
   const double codec_k = INT_ACC ? (448.0 / 127.0) * (448.0 / 127.0) : 1.0;
@@ -465,8 +472,8 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
     if (p.ksplit_cluster) {
       // one CTA per (tile, K slice); the slices of a tile form one cluster and
       // sum their raw tiles through distributed shared memory
-      using LK = GemmLayout<BN, 1, STAGES, 1, true>;
-      auto kk = umma_gemm_kernel<KIND, BN, 1, STAGES, Epi, B_MN, 1, true, kEpiWarps>;
+      using LK = GemmLayout<BN, 1, STAGES, 1, true, A_ROWS>;
+      auto kk = umma_gemm_kernel<KIND, BN, 1, STAGES, Epi, B_MN, 1, true, kEpiWarps, A_ROWS>;
       if (gemm_resident_units(reinterpret_cast<const void*>(kk), kThreads, LK::SMEM_BYTES, 1) <= 0)
         return cudaErrorInvalidConfiguration;
       typename Epi::Params epk = ep;
@@ -493,13 +500,14 @@ cudaError_t launch_fp8_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const 
   return cudaGetLastError();
 }
 
-template <MmaKind KIND, int BN, bool B_MN, int CG>
+template <MmaKind KIND, int BN, bool B_MN, int CG, int A_ROWS = 128>
 cudaError_t launch_fp8_out(const CUtensorMap& ta, const CUtensorMap& tb, const Fp8GemmArgs& g, const Fp8Plan& p,
                            uint32_t idesc, const int32_t* cr, const int32_t* cc, uint32_t* part, cudaStream_t st) {
   switch (g.out_dtype) {
-    case F16: return launch_fp8_gemm<KIND, BN, __half, B_MN, CG>(ta, tb, g, p, idesc, cr, cc, part, st);
-    case BF16: return launch_fp8_gemm<KIND, BN, __nv_bfloat16, B_MN, CG>(ta, tb, g, p, idesc, cr, cc, part, st);
-    default: return launch_fp8_gemm<KIND, BN, float, B_MN, CG>(ta, tb, g, p, idesc, cr, cc, part, st);
+    case F16: return launch_fp8_gemm<KIND, BN, __half, B_MN, CG, A_ROWS>(ta, tb, g, p, idesc, cr, cc, part, st);
+    case BF16:
+      return launch_fp8_gemm<KIND, BN, __nv_bfloat16, B_MN, CG, A_ROWS>(ta, tb, g, p, idesc, cr, cc, part, st);
+    default: return launch_fp8_gemm<KIND, BN, float, B_MN, CG, A_ROWS>(ta, tb, g, p, idesc, cr, cc, part, st);
   }
 }
 
@@ -510,7 +518,8 @@ cudaError_t launch_fp8_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Fp
     return p.cg == 2 ? launch_fp8_out<KIND, 256, B_MN, 2>(ta, tb, g, p, idesc, cr, cc, part, st)
                      : launch_fp8_out<KIND, 256, B_MN, 1>(ta, tb, g, p, idesc, cr, cc, part, st);
   }
-  return launch_fp8_out<KIND, 128, B_MN, 1>(ta, tb, g, p, idesc, cr, cc, part, st);
+  return p.a_rows == 32 ? launch_fp8_out<KIND, 128, B_MN, 1, 32>(ta, tb, g, p, idesc, cr, cc, part, st)
+                        : launch_fp8_out<KIND, 128, B_MN, 1>(ta, tb, g, p, idesc, cr, cc, part, st);
 }
 
 }  // namespace
@@ -537,7 +546,7 @@ void fp8_gemm_tile(int64_t M, int64_t N, int64_t K, int ab_dtype, int b_layout, 
   out[0] = 128 * p.cg;
   out[1] = p.bn;
   out[2] = p.cg;
-  out[3] = stages_for(p.bn, p.cg);
+  out[3] = stages_for(p.bn, p.cg, p.a_rows);
   out[4] = p.splits;
   out[5] = kGroupM;
 }
@@ -622,7 +631,8 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
 
   CUtensorMap ta, tb;
   const int64_t lda = p.legacy ? p.Kp : g.K;
-  if (!make_tmap_kmajor(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.M, lda, lda, 128)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&ta, a, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.M, lda, lda, static_cast<uint32_t>(p.a_rows)))
+    return cudaErrorInvalidValue;
   if (p.b_mn) {
     // [K, N] with N contiguous: boxes of 128 bytes of N x 128 K rows
     if (!make_tmap_kmajor(&tb, b, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, g.K, g.N, g.N, 128)) return cudaErrorInvalidValue;

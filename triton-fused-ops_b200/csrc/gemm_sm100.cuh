@@ -51,12 +51,18 @@ struct TileSched {
 };
 
 // Per-CTA shared-memory layout. The UMMA is M = 128 * CG by N = NUM_B *
-// BLOCK_N; each CTA stages 128 rows of A and N / CG rows of B per K block.
-template <int BLOCK_N, int NUM_B, int STAGES, int CG = 1, bool KSPLIT = false>
+// BLOCK_N; each CTA stages A_ROWS rows of A and N / CG rows of B per K block.
+// A_ROWS < 128 (one CTA per MMA, M <= A_ROWS): the A stages are packed
+// closer, so more stages fit; the MMA still reads 128 rows from a stage's
+// start, the rows past A_ROWS being whatever follows in shared memory (later
+// A stages, then the first B stage: always inside the allocation), and the
+// accumulator rows they feed lie past M and are never stored.
+template <int BLOCK_N, int NUM_B, int STAGES, int CG = 1, bool KSPLIT = false, int A_ROWS = 128>
 struct GemmLayout {
-  static constexpr int BM = 128;             // A rows (and accumulator lanes) per CTA
+  static constexpr int BM = 128;             // accumulator lanes (output rows) per CTA
   static constexpr int PAIR_M = BM * CG;     // rows per tile
-  static constexpr int A_BYTES = BM * 128;
+  static constexpr int A_BYTES = A_ROWS * 128;
+  static_assert(A_ROWS % 8 == 0 && A_ROWS <= BM && (A_ROWS == BM || CG == 1), "A stage rows");
   static constexpr int N_MMA = NUM_B * BLOCK_N;
   static constexpr int B_ROWS = N_MMA / CG;  // B rows staged by one CTA
   static constexpr int B_STAGE_BYTES = B_ROWS * 128;
@@ -79,6 +85,8 @@ struct GemmLayout {
   static constexpr int SUM_OFFSET = RED_BYTES;
   static constexpr int SUM_BYTES = KSPLIT ? (BM / 2) * N_MMA * 4 : 0;
   static_assert(RED_BYTES + SUM_BYTES <= RING_BYTES, "reduction tiles fit in the ring");
+  static_assert(STAGES * A_BYTES + STAGES * B_STAGE_BYTES >= (STAGES - 1) * A_BYTES + BM * 128,
+                "a 128-row read from the last A stage stays inside the ring");
   static constexpr int BAR_OFFSET = RING_BYTES;
   // dynamic shared memory: ring + barriers + 1 KB for manual alignment
   static constexpr size_t SMEM_BYTES = static_cast<size_t>(BAR_OFFSET) + 256 + 1024;
@@ -164,7 +172,7 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, vo
 // must provide add_partial and final_params). A second cluster barrier keeps
 // every tile readable until all CTAs are done. 2 <= k_splits <= 8.
 template <MmaKind KIND, int BLOCK_N, int NUM_B, int STAGES, class Epi, bool B_MN = false, int CG = 1,
-          bool KSPLIT = false, int EPI_WARPS = 4>
+          bool KSPLIT = false, int EPI_WARPS = 4, int A_ROWS = 128>
 __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
     umma_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b0,
                      const __grid_constant__ CUtensorMap tmap_b1, int M, int N, int K, int group_m, uint32_t idesc,
@@ -172,7 +180,7 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
   griddep_launch_dependents();  // a programmatic-dependent GEMM after this one may be scheduled as CTAs retire
   static_assert(!B_MN || (NUM_B == 1 && KindTraits<KIND>::ELEM == 1 && BLOCK_N % 128 == 0),
                 "MN-major B: 8-bit operands, one B operand, BLOCK_N a multiple of 128");
-  using L = GemmLayout<BLOCK_N, NUM_B, STAGES, CG, KSPLIT>;
+  using L = GemmLayout<BLOCK_N, NUM_B, STAGES, CG, KSPLIT, A_ROWS>;
   constexpr int KB_ELEMS = 128 / KindTraits<KIND>::ELEM;
 
   extern __shared__ uint8_t smem_raw[];

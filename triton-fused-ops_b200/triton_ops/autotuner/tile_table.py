@@ -75,7 +75,8 @@ def fp8_gemm_config(M: int, N: int, K: int, sms: int = B200_SMS, pair: bool = Tr
     splits = 1
     if tiles < units // 2:
         splits = max(1, min(num_k // 4, units // tiles))
-    stages = 6 if cg == 2 else (4 if bn == 256 else 7)  # 32 KB stages; 48 KB for 256 x 128 single-CTA tiles
+    # 32 KB stages; 48 KB for 128 x 256 single-CTA tiles; 20 KB (32-row A stages) for M <= 32
+    stages = 6 if cg == 2 else (4 if bn == 256 else (11 if M <= 32 else 7))
     return {"BLOCK_M": 128 * cg, "BLOCK_N": bn, "CTAS_PER_MMA": cg, "STAGES": stages,
             "SPLIT_K": splits, "GROUP_M": 16}
 
