@@ -217,6 +217,29 @@ TFO_API int tfo_fp8_linear(const void* x_codes, const void* w_codes, const float
                            const void* bias, int bias_dtype, void* out, int64_t M, int64_t N, int64_t K, int ab_dtype,
                            int gemm_dtype, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
 
+/* The prepared form of a reference-codec (TFO_DTYPE_U8) weight w_codes[N, K]
+ * for tfo_fp8_linear_prepared: w_s8[n, k] = w_codes[n, k] ^ 0x80 (the int8
+ * value u - 128, N x K bytes) and w_sums[n] = the sum over k of w_s8[n, :].
+ * K % 16 == 0 and all pointers 16-byte aligned. The result stays valid while
+ * the weight does: prepare once per weight, not per call.
+ * No counterpart in the reference (its fp8_gemm re-reads the uint8 codes on
+ * every call). */
+TFO_API int tfo_fp8_prepare_weight(const void* w_codes, int64_t N, int64_t K, void* w_s8, int32_t* w_sums,
+                                   void* stream);
+
+/* tfo_fp8_linear for reference-codec operands with the weight prepared by
+ * tfo_fp8_prepare_weight: the same output bits, with no per-call operand
+ * preparation (tfo_fp8_linear sign-flips the smaller operand and sums it on
+ * every call, a pass over the weight when M > N). x_codes [M, K] uint8,
+ * K % 16 == 0, 16-byte-aligned pointers; bias may be NULL (then out_dtype
+ * must equal gemm_dtype). Workspace: tfo_fp8_gemm_workspace_bytes(M, N, K,
+ * TFO_DTYPE_U8, TFO_B_NK).
+ * Replaces: FP8Linear.forward's GEMM + bias (triton_ops/kernels/fp8_gemm.py:293-309). */
+TFO_API int tfo_fp8_linear_prepared(const void* x_codes, const void* w_s8, const int32_t* w_sums,
+                                    const float* x_scale, const float* w_scale, const void* bias, int bias_dtype,
+                                    void* out, int64_t M, int64_t N, int64_t K, int gemm_dtype, int out_dtype,
+                                    void* workspace, size_t workspace_bytes, void* stream);
+
 /* Workspace bytes tfo_gated_mlp needs (non-zero only when an fp32 copy of an
  * operand is required, i.e. mixed or fp32 dtypes). */
 TFO_API size_t tfo_gated_mlp_workspace_bytes(int64_t M, int64_t N, int64_t K, int x_dtype, int w_dtype);

@@ -286,3 +286,51 @@ def test_fp8linear_bias_in_epilogue(cuda, M, xdt, bdt):
     ref = _gemm_codes(xq, lin.weight_fp8, xs, lin.weight_scale, xdt, _lib.B_NK) + lin.bias
     assert y.dtype == ref.dtype and y.shape == ref.shape
     assert torch.equal(y, ref)
+
+
+@pytest.mark.parametrize("M", [1, 16, 300, 2048])
+@pytest.mark.parametrize("with_bias", [False, True])
+def test_prepared_weight_linear_equals_linear(cuda, M, with_bias):
+    """tfo_fp8_linear_prepared (weight sign-flipped and summed once) gives tfo_fp8_linear's bits, for M on
+    both sides of N (where tfo_fp8_linear prepares A, and where it prepares the weight per call)."""
+    from triton_ops import _lib, quantize_fp8
+    from triton_ops.kernels.fp8_gemm import _linear_bias, _gemm_codes, _linear_prepared
+
+    N, K = 1024, 512
+    g = torch.Generator(device="cuda").manual_seed(M)
+    x = torch.randn(M, K, device="cuda", generator=g).half()
+    w = 0.05 * torch.randn(N, K, device="cuda", generator=g)
+    qx, sx = quantize_fp8(x)
+    qw, sw = quantize_fp8(w)
+    w_s8 = torch.empty(N, K, dtype=torch.int8, device="cuda")
+    sums = torch.empty(N, dtype=torch.int32, device="cuda")
+    _lib.call("tfo_fp8_prepare_weight", qw.data_ptr(), N, K, w_s8.data_ptr(), sums.data_ptr(), _lib.stream_of(qw))
+    ref_s8 = (qw.cpu().numpy().astype(np.int32) - 128).astype(np.int8)
+    np.testing.assert_array_equal(w_s8.cpu().numpy(), ref_s8)
+    np.testing.assert_array_equal(sums.cpu().numpy(), ref_s8.astype(np.int64).sum(axis=1))
+    bias = (0.1 * torch.randn(N, device="cuda", generator=g)).float() if with_bias else None
+    got = _linear_prepared(qx, w_s8, sums, sx, sw, bias, torch.float16)
+    want = (_linear_bias(qx, qw, sx, sw, bias, torch.float16) if with_bias
+            else _gemm_codes(qx, qw, sx, sw, torch.float16, _lib.B_NK))
+    assert got.dtype == want.dtype and torch.equal(got, want)
+    assert _lib.device_error_flags() == 0
+
+
+def test_fp8linear_prepared_and_unaligned_in_features(cuda):
+    """FP8Linear uses the prepared weight when in_features % 16 == 0 (equal to the explicit GEMM), the
+    per-call path otherwise; modifying weight_fp8 in place refreshes the prepared copy."""
+    from triton_ops import FP8Linear, fp8_gemm, quantize_fp8
+
+    torch.manual_seed(1)
+    for K in (256, 100):
+        lin = FP8Linear(K, 384, bias=True).cuda()
+        x = torch.randn(3, 7, K, device="cuda", dtype=torch.float16)
+        y = lin(x)
+        qx, sx = quantize_fp8(x.view(-1, K))
+        ref = fp8_gemm(qx, lin.weight_fp8.t().contiguous(), sx, lin.weight_scale) + lin.bias
+        assert torch.equal(y.view(-1, 384), ref)
+    lin2 = FP8Linear(256, 384, bias=False).cuda()
+    x2 = torch.randn(5, 256, device="cuda", dtype=torch.float16)
+    y1 = lin2(x2)
+    lin2.weight_fp8.fill_(128)  # in place (code 128 decodes to 0): the next forward must see it
+    assert torch.equal(lin2(x2), torch.zeros_like(y1))

@@ -29,6 +29,7 @@ int cuda_fail(cudaError_t e, const char* where) {
 }
 
 bool is_float_dtype(int d) { return d == F16 || d == BF16 || d == F32; }
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 std::mutex g_cache_mu;
 std::map<int, int> g_sm_count;
@@ -431,6 +432,46 @@ int tfo_fp8_linear(const void* x_codes, const void* w_codes, const float* x_scal
   g.bias = bias;
   g.bias_dtype = bias_dtype;
   g.round_dtype = gemm_dtype;
+  if (workspace_bytes < fp8_gemm_workspace_bytes(g) || !workspace)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": workspace smaller than tfo_fp8_gemm_workspace_bytes()");
+  const cudaError_t e = fp8_gemm_launch(g, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return TFO_OK;
+}
+
+int tfo_fp8_prepare_weight(const void* w_codes, int64_t N, int64_t K, void* w_s8, int32_t* w_sums, void* stream) {
+  const char* fn = "tfo_fp8_prepare_weight";
+  if (N < 0 || K <= 0 || K % 16 != 0) return fail(TFO_ERR_INVALID, std::string(fn) + ": need N >= 0 and K a positive multiple of 16");
+  if (N == 0) return TFO_OK;
+  if (!w_codes || !w_s8 || !w_sums) return fail(TFO_ERR_INVALID, std::string(fn) + ": NULL pointer");
+  if (!aligned16(w_codes) || !aligned16(w_s8)) return fail(TFO_ERR_INVALID, std::string(fn) + ": pointers must be 16-byte aligned");
+  const cudaError_t e = fp8_prepare_rows_launch(w_codes, N, K, w_s8, w_sums, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, fn);
+  return TFO_OK;
+}
+
+int tfo_fp8_linear_prepared(const void* x_codes, const void* w_s8, const int32_t* w_sums, const float* x_scale,
+                            const float* w_scale, const void* bias, int bias_dtype, void* out, int64_t M, int64_t N,
+                            int64_t K, int gemm_dtype, int out_dtype, void* workspace, size_t workspace_bytes,
+                            void* stream) {
+  const char* fn = "tfo_fp8_linear_prepared";
+  if (!is_float_dtype(gemm_dtype) || !is_float_dtype(out_dtype) || (bias != nullptr && !is_float_dtype(bias_dtype)))
+    return fail(TFO_ERR_DTYPE, std::string(fn) + ": gemm, bias and output dtypes must be f16, bf16 or f32");
+  if (bias == nullptr && out_dtype != gemm_dtype)
+    return fail(TFO_ERR_DTYPE, std::string(fn) + ": without a bias the output dtype is gemm_dtype");
+  if (M < 0 || N < 0 || K <= 0 || K % 16 != 0)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": bad dimension (K must be a positive multiple of 16)");
+  if (M > INT32_MAX || N > INT32_MAX || K > 131072)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": M, N must fit in int32 and K <= 131072");
+  if (M == 0 || N == 0) return TFO_OK;
+  if (!x_codes || !w_s8 || !w_sums || !x_scale || !w_scale || !out)
+    return fail(TFO_ERR_INVALID, std::string(fn) + ": NULL pointer");
+  if (!aligned16(x_codes) || !aligned16(w_s8)) return fail(TFO_ERR_INVALID, std::string(fn) + ": operands must be 16-byte aligned");
+  Fp8GemmArgs g{x_codes, w_s8, x_scale, w_scale, out, M, N, K, U8, TFO_B_NK, out_dtype, workspace, workspace_bytes};
+  g.bias = bias;
+  g.bias_dtype = bias != nullptr ? bias_dtype : -1;
+  g.round_dtype = bias != nullptr ? gemm_dtype : -1;
+  g.b_s8_sums = w_sums;
   if (workspace_bytes < fp8_gemm_workspace_bytes(g) || !workspace)
     return fail(TFO_ERR_INVALID, std::string(fn) + ": workspace smaller than tfo_fp8_gemm_workspace_bytes()");
   const cudaError_t e = fp8_gemm_launch(g, static_cast<cudaStream_t>(stream));

@@ -168,7 +168,15 @@ struct Fp8GemmArgs {
   // per-token / per-channel scales: sa_rows[M] replaces sa, sb_cols[N] replaces sb
   const float* sa_rows = nullptr;
   const float* sb_cols = nullptr;
+  // reference codec, B given as [N, K] int8 values u - 128 (a prepared
+  // constant weight) with b_s8_sums[n] = their sum over k: A is used raw and
+  // no operand is prepared per call
+  const int32_t* b_s8_sums = nullptr;
 };
+// The prepared form of a [rows, K] reference-codec weight: dst = codes ^ 0x80
+// (int8 u - 128), sums[r] = the row's sum of those values.
+cudaError_t fp8_prepare_rows_launch(const void* codes, int64_t rows, int64_t K, void* dst, int32_t* sums,
+                                    cudaStream_t st);
 size_t fp8_gemm_workspace_bytes(const Fp8GemmArgs& g);
 // Launch choice of tfo_fp8_gemm for 16-byte-aligned operands: out = {rows
 // per tile, columns per tile, CTAs per MMA, stages, K splits, group_m}.

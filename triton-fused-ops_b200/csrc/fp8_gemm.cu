@@ -524,6 +524,15 @@ cudaError_t launch_fp8_bn(const CUtensorMap& ta, const CUtensorMap& tb, const Fp
 
 }  // namespace
 
+cudaError_t fp8_prepare_rows_launch(const void* codes, int64_t rows, int64_t K, void* dst, int32_t* sums,
+                                    cudaStream_t st) {
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((rows + 7) / 8, num_sms() * 8)));
+  prep_rows_s8_sum_kernel<<<grid, 256, 0, st>>>(static_cast<const uint8_t*>(codes), rows, K, static_cast<int8_t*>(dst),
+                                                 sums);
+  note_launch();
+  return cudaGetLastError();
+}
+
 // Upper bound over operand alignments.
 size_t fp8_gemm_workspace_bytes(const Fp8GemmArgs& g) {
   Fp8GemmArgs u = g;
@@ -586,7 +595,7 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
       note_launch();
     }
     b = db;
-  } else if (codec && p.prep_a) {
+  } else if (codec && p.prep_a && g.b_s8_sums == nullptr) {
     int32_t* sums = reinterpret_cast<int32_t*>(ws + p.off_sum);
     int8_t* da = reinterpret_cast<int8_t*>(ws + p.off_a);
     const int grid = static_cast<int>(std::min<int64_t>((g.M + 7) / 8, num_sms() * 8));
@@ -596,6 +605,10 @@ cudaError_t fp8_gemm_launch(const Fp8GemmArgs& g, cudaStream_t st) {
     a = reinterpret_cast<const uint8_t*>(da);
     corr_row = sums;
     b_fmt = 0;  // B stays raw u8
+  } else if (codec && g.b_s8_sums != nullptr) {
+    // B prepared once by the caller: A raw u8 x B int8, corrected per column
+    corr_col = g.b_s8_sums;
+    a_fmt = 0;
   } else if (codec && p.prep_b) {
     int32_t* sums = reinterpret_cast<int32_t*>(ws + p.off_sum);
     int8_t* db = reinterpret_cast<int8_t*>(ws + p.off_b);

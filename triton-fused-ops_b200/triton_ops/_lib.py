@@ -88,6 +88,12 @@ _SIGNATURES = {
         [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_int, _c_vp,
          _c_size, _c_vp],
     ),
+    "tfo_fp8_prepare_weight": (_c_int, [_c_vp, _c_i64, _c_i64, _c_vp, _c_vp, _c_vp]),
+    "tfo_fp8_linear_prepared": (
+        _c_int,
+        [_c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_vp, _c_int, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int, _c_vp,
+         _c_size, _c_vp],
+    ),
     "tfo_gated_mlp_quantize_workspace_bytes": (_c_size, [_c_vp, _c_vp, _c_vp, _c_i64, _c_i64, _c_i64, _c_int, _c_int,
                                                           _c_int]),
     "tfo_gated_mlp_quantize": (

@@ -109,6 +109,28 @@ def _linear_bias(x_codes, w_codes, x_scale, w_scale, bias, gemm_dtype):
     return out
 
 
+def _linear_prepared(x_codes, w_s8, w_sums, x_scale, w_scale, bias, gemm_dtype):
+    """FP8Linear's GEMM (+ bias in the epilogue) on reference-codec codes with the weight prepared once
+    (``tfo_fp8_prepare_weight``): the same values as :func:`_linear_bias` / :func:`_gemm_codes`, with no
+    per-call operand preparation."""
+    M, K = x_codes.shape
+    N = w_s8.shape[0]
+    res_dtype = gemm_dtype if bias is None else torch.promote_types(gemm_dtype, bias.dtype)
+    out = torch.empty(M, N, dtype=res_dtype, device=x_codes.device)
+    if out.numel() == 0:
+        return out
+    b = None if bias is None else bias.to(x_codes.device).contiguous()
+    ws = _lib.workspace(_lib.load().tfo_fp8_gemm_workspace_bytes(M, N, K, _lib.U8, _lib.B_NK), x_codes.device)
+    _lib.call(
+        "tfo_fp8_linear_prepared", x_codes.data_ptr(), w_s8.data_ptr(), w_sums.data_ptr(),
+        _scale_f32(x_scale.to(x_codes.device)).data_ptr(), _scale_f32(w_scale.to(x_codes.device)).data_ptr(),
+        None if b is None else b.data_ptr(), -1 if b is None else _lib.dtype_code(b.dtype, "bias"), out.data_ptr(),
+        M, N, K, _lib.dtype_code(gemm_dtype), _lib.dtype_code(res_dtype), ws.data_ptr(), ws.numel(),
+        _lib.stream_of(x_codes),
+    )
+    return out
+
+
 def fp8_gemm(
     a: torch.Tensor,
     b: torch.Tensor,
@@ -177,6 +199,7 @@ class FP8Linear(torch.nn.Module):
         else:
             self.register_parameter("bias", None)
         self._quantized = False
+        self._prepared = None  # (key, int8 weight, row sums): the weight's form for tfo_fp8_linear_prepared
 
     def quantize_weights(self):
         """Quantizes the weight once (reference codec, per-tensor scale)."""
@@ -185,6 +208,20 @@ class FP8Linear(torch.nn.Module):
             self.weight_fp8 = weight_fp8
             self.weight_scale = weight_scale
             self._quantized = True
+
+    def _prepared_weight(self):
+        """The weight codes as int8 (u - 128) with their row sums, made once per weight tensor (and again
+        only if ``weight_fp8`` is replaced or modified in place)."""
+        w = self.weight_fp8
+        key = (w.data_ptr(), w._version, w.device)
+        if self._prepared is None or self._prepared[0] != key:
+            N, K = w.shape
+            w_s8 = torch.empty(N, K, dtype=torch.int8, device=w.device)
+            sums = torch.empty(N, dtype=torch.int32, device=w.device)
+            _lib.call("tfo_fp8_prepare_weight", w.data_ptr(), N, K, w_s8.data_ptr(), sums.data_ptr(),
+                      _lib.stream_of(w))
+            self._prepared = (key, w_s8, sums)
+        return self._prepared[1], self._prepared[2]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         self.quantize_weights()
@@ -195,7 +232,14 @@ class FP8Linear(torch.nn.Module):
         x_fp8, x_scale = quantize_fp8(x_2d)
         out_dtype = x.dtype if x.dtype in SUPPORTED_DTYPES_FLOAT else torch.float16
         # weight_fp8 is [out, in] = [N, K]: consumed directly as the K-major B operand.
-        if self.bias is None:
+        w = self.weight_fp8
+        if (w.dtype == torch.uint8 and x_fp8.dtype == torch.uint8 and self.in_features % 16 == 0
+                and w.is_contiguous() and w.data_ptr() % 16 == 0 and x_fp8.data_ptr() % 16 == 0
+                and w.device == x_fp8.device):
+            # the weight prepared once: no per-call operand preparation
+            w_s8, sums = self._prepared_weight()
+            output = _linear_prepared(x_fp8, w_s8, sums, x_scale, self.weight_scale, self.bias, out_dtype)
+        elif self.bias is None:
             output = _gemm_codes(x_fp8, self.weight_fp8, x_scale, self.weight_scale, out_dtype, _lib.B_NK)
         else:
             output = _linear_bias(x_fp8, self.weight_fp8, x_scale, self.weight_scale, self.bias, out_dtype)
