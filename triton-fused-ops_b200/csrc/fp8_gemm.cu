@@ -207,11 +207,51 @@ __device__ __forceinline__ float round_to_dtype(float v, int dt) {
   if (dt == BF16) return __bfloat162float(__float2bfloat16_rn(v));
   return v;
 }
+// The 16 bias values of columns col0.. as fp32: 16-byte loads when all 16
+// exist and are 16-byte aligned (col0 is a multiple of 16), else one by one.
+__device__ __forceinline__ void load_bias16(float (&b)[16], const void* bias, int bias_dt, int col0, int valid) {
+  const int esz = bias_dt == F32 ? 4 : 2;
+  const uint8_t* p = static_cast<const uint8_t*>(bias) + static_cast<int64_t>(col0) * esz;
+  if (valid == 16 && (reinterpret_cast<uintptr_t>(p) & 15u) == 0) {
+    if (bias_dt == F32) {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(p) + q);
+        b[4 * q] = t.x; b[4 * q + 1] = t.y; b[4 * q + 2] = t.z; b[4 * q + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const uint4 t = __ldg(reinterpret_cast<const uint4*>(p) + q);
+        const uint32_t w[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 f = bias_dt == F16 ? __half22float2(*reinterpret_cast<const __half2*>(&w[j]))
+                                          : __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&w[j]));
+          b[8 * q + 2 * j] = f.x;
+          b[8 * q + 2 * j + 1] = f.y;
+        }
+      }
+    }
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) b[i] = i < valid ? load_as_float(bias, col0 + i, bias_dt) : 0.f;
+  }
+}
 __device__ __forceinline__ void linear_bias16(float (&v)[16], const void* bias, int bias_dt, int round_dt, int col0,
                                               int valid) {
+  float b[16];
+  load_bias16(b, bias, bias_dt, col0, valid);
+  // the product rounded to the GEMM's output dtype (one branch per call), then the bias in fp32
+  if (round_dt == F16) {
 #pragma unroll
-  for (int i = 0; i < 16; ++i)
-    if (i < valid) v[i] = __fadd_rn(round_to_dtype(v[i], round_dt), load_as_float(bias, col0 + i, bias_dt));
+    for (int i = 0; i < 16; ++i) v[i] = __half2float(__float2half_rn(v[i]));
+  } else if (round_dt == BF16) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) v[i] = __bfloat162float(__float2bfloat16_rn(v[i]));
+  }
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __fadd_rn(v[i], b[i]);
 }
 
 template <typename TO, bool INT_ACC>
