@@ -748,12 +748,30 @@ cudaError_t quant_small_t(const void* x, int64_t n, float* scale_out, void* out,
   return e;
 }
 
+// Mid-size tensors (above the one-cluster form, up to kMidMaxBytes): two
+// ordinary launches, per-CTA amax partials then an encode that reduces them
+// (re-reading x, from L2 at these sizes). No barrier memset, no cooperative
+// launch: at [1024, 4096] fp16 8.3 us against 14.2 us for the resident form,
+// which only pays off once x is large enough for its single HBM read to
+// matter.
+constexpr int64_t kMidMaxBytes = 16ll << 20;
+
 template <typename T, bool E4M3>
 cudaError_t quant_any_t(const void* x, int64_t n, float* scale_out, void* out, void* ws, size_t ws_bytes,
                         cudaStream_t st) {
   bool used = false;
   cudaError_t e = quant_small_t<T, E4M3>(x, n, scale_out, out, st, &used);
   if (e != cudaSuccess || used) return e;
+  if (n * static_cast<int64_t>(sizeof(T)) <= kMidMaxBytes) {
+    const int nparts = amax_partials_count(n);
+    if (ws_bytes < static_cast<size_t>(nparts) * sizeof(uint32_t)) return cudaErrorInvalidValue;
+    uint32_t* parts = static_cast<uint32_t*>(ws);
+    const int x_dtype = std::is_same<T, float>::value ? F32 : (std::is_same<T, __half>::value ? F16 : BF16);
+    e = amax_partials_launch(x, n, x_dtype, parts, nparts, st);
+    if (e != cudaSuccess) return e;
+    return encode_launch(x, n, x_dtype, nullptr, parts, nparts, scale_out, out,
+                         E4M3 ? static_cast<int>(DType::E4M3) : static_cast<int>(DType::U8), st);
+  }
   e = quant_res_t<T, E4M3>(x, n, scale_out, out, ws, ws_bytes, st, &used);
   if (e != cudaSuccess || used) return e;
   return quant_dyn_t<T, E4M3>(x, n, scale_out, out, ws, ws_bytes, st);
