@@ -153,6 +153,7 @@ constexpr int kAmaxThreads = 256;
 template <typename T>
 __global__ void __launch_bounds__(kAmaxThreads) amax_partial_kernel(const T* __restrict__ x, int64_t n, bool vec,
                                                                      uint32_t* __restrict__ partials) {
+  griddep_launch_dependents();  // the encode that follows may be scheduled early
   __shared__ uint32_t red[32];
   const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
@@ -175,6 +176,7 @@ __global__ void __launch_bounds__(kEncThreads) encode_kernel(const T* __restrict
                                                              const uint32_t* __restrict__ partials, int nparts,
                                                              float* __restrict__ scale_out, uint8_t* __restrict__ out) {
   griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
+  griddep_wait();               // launched as a programmatic dependent: inputs are read after this
   __shared__ float s_sh;
   __shared__ uint32_t red[32];
   if (partials != nullptr) {
@@ -621,15 +623,14 @@ static cudaError_t enc_t(const void* x, int64_t n, const float* scale_in, const 
   const void* kern = (out_dtype == E4M3) ? reinterpret_cast<const void*>(encode_kernel<T, true>)
                                          : reinterpret_cast<const void*>(encode_kernel<T, false>);
   const int grid = grid_for(std::max<int64_t>(n / 32, 1), kEncThreads, cached_occupancy(kern, kEncThreads, 0));
-  if (out_dtype == E4M3) {
-    encode_kernel<T, true><<<grid, kEncThreads, 0, st>>>(static_cast<const T*>(x), n, vec, scale_in, partials, nparts,
-                                                         scale_out, static_cast<uint8_t*>(out));
-  } else {
-    encode_kernel<T, false><<<grid, kEncThreads, 0, st>>>(static_cast<const T*>(x), n, vec, scale_in, partials, nparts,
-                                                          scale_out, static_cast<uint8_t*>(out));
-  }
+  // a programmatic dependent of the kernel before it (e.g. the amax partials)
+  cudaError_t e = (out_dtype == E4M3)
+                      ? launch_dependent(encode_kernel<T, true>, grid, kEncThreads, st, static_cast<const T*>(x), n,
+                                         vec, scale_in, partials, nparts, scale_out, static_cast<uint8_t*>(out))
+                      : launch_dependent(encode_kernel<T, false>, grid, kEncThreads, st, static_cast<const T*>(x), n,
+                                         vec, scale_in, partials, nparts, scale_out, static_cast<uint8_t*>(out));
   note_launch();
-  return cudaGetLastError();
+  return e;
 }
 
 cudaError_t encode_launch(const void* x, int64_t n, int x_dtype, const float* scale_in, const uint32_t* partials,
