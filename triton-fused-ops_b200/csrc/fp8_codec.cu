@@ -523,7 +523,7 @@ template <typename TO, bool E4M3>
 __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __restrict__ q, int64_t n, bool vec,
                                                              const float* __restrict__ scale, TO* __restrict__ out) {
   using R = typename Raw<TO>::type;
-  constexpr int U = 4;  // 16-byte code vectors in flight per thread
+  constexpr int U = 8;  // 16-byte code vectors in flight per thread
   // One copy of the 256 outputs per lane (lut[u * 32 + lane]), so the
   // data-dependent lookups of a warp never collide on a shared-memory bank.
   __shared__ R base[256];
@@ -804,7 +804,7 @@ static cudaError_t dec_t(const void* q, int64_t n, bool e4m3, const float* scale
   const void* kern = e4m3 ? reinterpret_cast<const void*>(decode_kernel<TO, true>)
                           : reinterpret_cast<const void*>(decode_kernel<TO, false>);
   const int per_sm = cached_occupancy(kern, kDecThreads, 0);
-  const int grid = grid_for(std::max<int64_t>(n / 64, 1), kDecThreads, per_sm);
+  const int grid = grid_for(std::max<int64_t>(n / 128, 1), kDecThreads, per_sm);
   if (e4m3) {
     decode_kernel<TO, true><<<grid, kDecThreads, 0, st>>>(static_cast<const uint8_t*>(q), n, vec, scale, static_cast<TO*>(out));
   } else {
