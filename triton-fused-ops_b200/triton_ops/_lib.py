@@ -209,6 +209,24 @@ def version() -> str:
     return load().tfo_version().decode()
 
 
+# One grow-only scratch buffer per (device, stream): calls on one stream run in
+# order, so each may reuse the buffer of the one before. (A fresh tensor from
+# torch's caching allocator costs ~2 us of host time per call.) While a CUDA
+# graph is being captured a fresh tensor is taken instead, so that no buffer
+# is shared between a graph's private pool and eager calls.
+_ws_cache: dict = {}
+_is_capturing = getattr(torch.cuda, "is_current_stream_capturing", lambda: False)
+
+
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
-    """A scratch buffer from torch's caching allocator (at least 16 bytes)."""
-    return torch.empty(max(int(nbytes), 16), dtype=torch.uint8, device=device)
+    """A scratch buffer of at least `nbytes` (and 16) bytes on `device` for the current stream."""
+    n = max(int(nbytes), 16)
+    if _is_capturing():
+        return torch.empty(n, dtype=torch.uint8, device=device)
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    key = (idx, _raw_stream(idx) if _raw_stream is not None else torch.cuda.current_stream(idx).cuda_stream)
+    buf = _ws_cache.get(key)
+    if buf is None or buf.numel() < n:
+        buf = torch.empty(max(n, 2 * buf.numel() if buf is not None else n), dtype=torch.uint8, device=device)
+        _ws_cache[key] = buf
+    return buf

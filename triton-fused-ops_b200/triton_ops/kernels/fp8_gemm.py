@@ -119,11 +119,16 @@ def _linear_prepared(x_codes, w_s8, w_sums, x_scale, w_scale, bias, gemm_dtype):
     out = torch.empty(M, N, dtype=res_dtype, device=x_codes.device)
     if out.numel() == 0:
         return out
-    b = None if bias is None else bias.to(x_codes.device).contiguous()
-    ws = _lib.workspace(_lib.load().tfo_fp8_gemm_workspace_bytes(M, N, K, _lib.U8, _lib.B_NK), x_codes.device)
+    dev = x_codes.device
+
+    def on_dev(t):
+        return t if t.device == dev else t.to(dev)
+
+    b = None if bias is None else on_dev(bias).contiguous()
+    ws = _lib.workspace(_lib.load().tfo_fp8_gemm_workspace_bytes(M, N, K, _lib.U8, _lib.B_NK), dev)
     _lib.call(
         "tfo_fp8_linear_prepared", x_codes.data_ptr(), w_s8.data_ptr(), w_sums.data_ptr(),
-        _scale_f32(x_scale.to(x_codes.device)).data_ptr(), _scale_f32(w_scale.to(x_codes.device)).data_ptr(),
+        _scale_f32(on_dev(x_scale)).data_ptr(), _scale_f32(on_dev(w_scale)).data_ptr(),
         None if b is None else b.data_ptr(), -1 if b is None else _lib.dtype_code(b.dtype, "bias"), out.data_ptr(),
         M, N, K, _lib.dtype_code(gemm_dtype), _lib.dtype_code(res_dtype), ws.data_ptr(), ws.numel(),
         _lib.stream_of(x_codes),
