@@ -295,3 +295,21 @@ def test_one_cluster_form_nan_inf_and_zero(cuda):
         s_ref = O.compute_scale(x)
         assert f32bits(s.item()) == f32bits(s_ref)
         np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(x, s_ref))
+
+
+@pytest.mark.parametrize("n,launches", [((8 << 20) - 8, 2), (8 << 20, 2), ((8 << 20) + 8, 2)])
+def test_dynamic_scale_partials_and_resident_boundary(cuda, n, launches):
+    """fp16 tensors of up to 16 MB use amax partials + encode (two launches); above, the resident form
+    (barrier memset + one cooperative launch, also two). Same bytes as the oracle on both sides."""
+    from triton_ops import _lib, quantize_fp8
+
+    rng = np.random.default_rng(n % 1000)
+    x = O.round_to((rng.standard_normal(n) * 5).astype(np.float32), "f16")
+    xt = dev_tensor(x, "f16")
+    n0 = _lib.kernel_launches()
+    q, s = quantize_fp8(xt)
+    assert _lib.kernel_launches() - n0 == launches
+    s_ref = O.compute_scale(x)
+    assert f32bits(s.item()) == f32bits(s_ref)
+    np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(x, s_ref))
+    assert _lib.device_error_flags() == 0
