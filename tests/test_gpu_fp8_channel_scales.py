@@ -85,3 +85,44 @@ def test_gemm_with_token_and_channel_scales(cuda, M, code):
     out1 = host(fp8_gemm(qa, qb1, sa, sb1, torch.float32))
     ref1 = (dec(qa) / host(sa).astype(np.float64)) @ (dec(qb1) / float(sb1.item()))
     assert O.rel_fro(out1, ref1) <= 1e-5
+
+
+@pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
+@pytest.mark.parametrize("rows,cols", [(1, 16), (3, 48), (37, 1040), (16, 4096)])
+def test_per_row_vector_and_scalar_paths(cuda, dt, rows, cols):
+    """Rows of whole 16-element chunks on 16-byte boundaries take the vectorised per-row kernels;
+    the same values one element off a 16-byte boundary take the element-wise ones. Both equal the
+    oracle (codes, decoded values) and torch's expression (scales), NaN/inf elements and a zero
+    row included."""
+    from triton_ops import FP8Format, dequantize_fp8, quantize_fp8
+
+    tdt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[dt]
+    g = torch.Generator().manual_seed(rows * cols)
+    x = (torch.randn(rows, cols, generator=g) * torch.logspace(-2, 2, rows)[:, None]).to(tdt).cuda()
+    if rows > 2:
+        x[rows // 2] = 0
+    s = FP8Format.compute_scale_per_channel(x, dim=-1)
+    assert torch.equal(s, torch_per_channel(x, -1))
+    s32 = s.float()
+    xs = x.clone()
+    xs[0, 1] = float("inf")
+    xs[0, cols - 1] = float("nan")
+    flat = torch.empty(rows * cols + 8, dtype=tdt, device="cuda")
+    off = flat[1:1 + rows * cols].view(rows, cols)  # 2 or 4 bytes past a 16-byte boundary
+    off.copy_(xs)
+    xn, sn = host(xs), host(s32)
+    for src in (xs, off):
+        q, _ = quantize_fp8(src, s32)
+        np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(xn, sn))
+        for od, name in ((torch.float16, "f16"), (torch.float32, "f32"), (torch.bfloat16, "bf16")):
+            np.testing.assert_array_equal(host(dequantize_fp8(q, s32, od)), O.dequantize_ref(q.cpu().numpy(), sn, name))
+        q8, _ = quantize_fp8(src, s32, dtype=torch.float8_e4m3fn)
+        ref8 = (xs.float() * s32).clamp(-448, 448).to(torch.float8_e4m3fn)
+        assert torch.equal(q8.view(torch.uint8), ref8.view(torch.uint8))
+        d8 = dequantize_fp8(q8, s32, torch.float32)
+        torch.testing.assert_close(d8, ref8.float() / s32, rtol=0, atol=0, equal_nan=True)
+    qo = torch.empty(rows * cols + 16, dtype=torch.uint8, device="cuda")[3:3 + rows * cols].view(rows, cols)
+    q, _ = quantize_fp8(xs, s32)
+    qo.copy_(q)
+    np.testing.assert_array_equal(host(dequantize_fp8(qo, s32, torch.float32)),
+                                  O.dequantize_ref(q.cpu().numpy(), sn, "f32"))

@@ -437,75 +437,7 @@ __global__ void __launch_bounds__(kSmallThreads, 1)
   }
 }
 
-// ---- per-row (per-token / per-channel) scales ------------------------------
-// One warp per row of a [rows, cols] matrix (row-major, contiguous).
-constexpr int kRowThreads = 256;
-
-// scales[r] = 448 / max|x[r, :]| as FP8Format.compute_scale_per_channel
-// (triton_ops/models.py:301-314) evaluates it in torch: a zero max counts as
-// 1, and `448.0 / t` is `t.reciprocal() * 448`, each step rounded to x's dtype
-// (computed in fp32 first). The value is stored as fp32.
-template <typename T>
-__global__ void __launch_bounds__(kRowThreads) row_scales_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
-                                                                 float* __restrict__ scales) {
-  const int lane = threadIdx.x & 31;
-  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x) >> 5; r < rows;
-       r += (static_cast<int64_t>(gridDim.x) * kRowThreads) >> 5) {
-    uint32_t m = 0;
-    const T* xr = x + r * cols;
-    for (int64_t c = lane; c < cols; c += 32) m = max(m, __float_as_uint(fabsf(Ty<T>::to_f(xr[c]))));
-    m = warp_max_u32(m);
-    if (lane == 0) {
-      const float amax = __uint_as_float(m);
-      const float rcp = Ty<T>::to_f(Ty<T>::from_f(__frcp_rn(amax == 0.f ? 1.0f : amax)));
-      scales[r] = Ty<T>::to_f(Ty<T>::from_f(__fmul_rn(rcp, 448.0f)));
-    }
-  }
-}
-
-// Codes of x[r, c] * scales[r] (reference codec: clamp, NaN kept; or e4m3).
-template <typename T, bool E4M3>
-__global__ void __launch_bounds__(kRowThreads) encode_rows_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
-                                                                  const float* __restrict__ scales,
-                                                                  uint8_t* __restrict__ out) {
-  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
-  const int64_t n = rows * cols;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * kRowThreads) {
-    const float c = __fmul_rn(Ty<T>::to_f(x[i]), __ldg(scales + i / cols));
-    out[i] = static_cast<uint8_t>(E4M3 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(c, __NV_SATFINITE, __NV_E4M3))
-                                       : ref_encode(c));
-  }
-}
-
-// out[r, c] = dec(q[r, c]) / scales[r], dec as in the per-tensor decode.
-template <typename TO, bool E4M3>
-__global__ void __launch_bounds__(kRowThreads) decode_rows_kernel(const uint8_t* __restrict__ q, int64_t rows,
-                                                                  int64_t cols, const float* __restrict__ scales,
-                                                                  TO* __restrict__ out) {
-  __shared__ float dec[256];
-  for (int u = threadIdx.x; u < 256; u += kRowThreads) {
-    if constexpr (E4M3) {
-      __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(u), __NV_E4M3);
-      dec[u] = __half2float(__half(hr));
-    } else {
-      dec[u] = __fmul_rn(__fdiv_rn(static_cast<float>(u - 128), 127.0f), 448.0f);
-    }
-  }
-  __syncthreads();
-  const int64_t n = rows * cols;
-  for (int64_t i = static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x; i < n;
-       i += static_cast<int64_t>(gridDim.x) * kRowThreads)
-    out[i] = Ty<TO>::from_f(__fdiv_rn(dec[q[i]], __ldg(scales + i / cols)));
-}
-
-// ---- decode ----------------------------------------------------------------
-constexpr int kDecThreads = 512;
-
-// out = RN_out( dec(u) / s ), dec(u) = RN(RN(float(u - 128) / 127) * 448) for
-// the reference codec (triton_ops/kernels/fp8_quantize.py:305-312) or the
-// e4m3 value of u. Only 256 outputs exist per call, so each CTA builds them
-// in shared memory and the stream becomes a table lookup.
+// Bit pattern of v rounded to TO (16 bits for fp16/bf16, 32 for fp32).
 template <typename TO> struct Raw { using type = uint16_t; };
 template <> struct Raw<float> { using type = uint32_t; };
 
@@ -519,6 +451,150 @@ __device__ __forceinline__ typename Raw<TO>::type to_raw(float v) {
   }
 }
 
+// ---- per-row (per-token / per-channel) scales ------------------------------
+// One warp per row of a [rows, cols] matrix (row-major, contiguous).
+constexpr int kRowThreads = 256;
+
+// scales[r] = 448 / max|x[r, :]| as FP8Format.compute_scale_per_channel
+// (triton_ops/models.py:301-314) evaluates it in torch: a zero max counts as
+// 1, and `448.0 / t` is `t.reciprocal() * 448`, each step rounded to x's dtype
+// (computed in fp32 first). The value is stored as fp32.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) row_scales_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+                                                                 bool vec, float* __restrict__ scales) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x) >> 5; r < rows;
+       r += (static_cast<int64_t>(gridDim.x) * kRowThreads) >> 5) {
+    uint32_t m = 0;
+    const T* xr = x + r * cols;
+    if (vec) {  // rows of whole 16-element chunks, 16-byte aligned: two chunks in flight per lane
+      const int64_t cpr = cols / 16;
+      for (int64_t c = lane; c < cpr; c += 64) {
+        Chunk<T> a, b;
+        a.template load<false>(xr + c * 16);
+        if (c + 32 < cpr) b.template load<false>(xr + (c + 32) * 16);
+        else b.zero();
+        float f[16];
+        a.to_f(f);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) m = max(m, __float_as_uint(fabsf(f[j])));
+        b.to_f(f);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) m = max(m, __float_as_uint(fabsf(f[j])));
+      }
+    } else {
+      for (int64_t c = lane; c < cols; c += 32) m = max(m, __float_as_uint(fabsf(Ty<T>::to_f(xr[c]))));
+    }
+    m = warp_max_u32(m);
+    if (lane == 0) {
+      const float amax = __uint_as_float(m);
+      const float rcp = Ty<T>::to_f(Ty<T>::from_f(__frcp_rn(amax == 0.f ? 1.0f : amax)));
+      scales[r] = Ty<T>::to_f(Ty<T>::from_f(__fmul_rn(rcp, 448.0f)));
+    }
+  }
+}
+
+// Codes of x[r, c] * scales[r] (reference codec: clamp, NaN kept; or e4m3).
+// VEC: x and out 16-byte aligned and cols a multiple of 16, so each thread
+// takes one 16-element chunk (one row, one scale) and stores 16 codes at once.
+template <typename T, bool E4M3>
+__global__ void __launch_bounds__(kRowThreads) encode_rows_kernel(const T* __restrict__ x, int64_t rows, int64_t cols,
+                                                                  bool vec, const float* __restrict__ scales,
+                                                                  uint8_t* __restrict__ out) {
+  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
+  auto enc1 = [](float c) -> uint32_t {
+    return E4M3 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(c, __NV_SATFINITE, __NV_E4M3)) : ref_encode(c);
+  };
+  const int64_t n = rows * cols;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kRowThreads;
+  if (vec) {
+    const int64_t cpr = cols / 16;
+    for (int64_t i = tid; i < n / 16; i += stride) {
+      Chunk<T> c;
+      c.template load<true>(x + i * 16);
+      const float s = __ldg(scales + i / cpr);
+      float f[16];
+      c.to_f(f);
+      uint32_t w[4];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if constexpr (E4M3) {
+          const uint32_t lo = __nv_cvt_float2_to_fp8x2(
+              make_float2(__fmul_rn(f[4 * q], s), __fmul_rn(f[4 * q + 1], s)), __NV_SATFINITE, __NV_E4M3);
+          const uint32_t hi = __nv_cvt_float2_to_fp8x2(
+              make_float2(__fmul_rn(f[4 * q + 2], s), __fmul_rn(f[4 * q + 3], s)), __NV_SATFINITE, __NV_E4M3);
+          w[q] = lo | (hi << 16);
+        } else {
+          w[q] = enc1(__fmul_rn(f[4 * q], s)) | (enc1(__fmul_rn(f[4 * q + 1], s)) << 8) |
+                 (enc1(__fmul_rn(f[4 * q + 2], s)) << 16) | (enc1(__fmul_rn(f[4 * q + 3], s)) << 24);
+        }
+      }
+      __stcs(reinterpret_cast<uint4*>(out) + i, make_uint4(w[0], w[1], w[2], w[3]));
+    }
+    return;
+  }
+  for (int64_t i = tid; i < n; i += stride)
+    out[i] = static_cast<uint8_t>(enc1(__fmul_rn(Ty<T>::to_f(x[i]), __ldg(scales + i / cols))));
+}
+
+// out[r, c] = dec(q[r, c]) / scales[r], dec as in the per-tensor decode.
+// VEC: q and out 16-byte aligned and cols a multiple of 16, so each thread
+// takes one 16-code vector (one row, one scale) and stores its outputs as
+// 16-byte vectors.
+template <typename TO, bool E4M3>
+__global__ void __launch_bounds__(kRowThreads) decode_rows_kernel(const uint8_t* __restrict__ q, int64_t rows,
+                                                                  int64_t cols, bool vec,
+                                                                  const float* __restrict__ scales,
+                                                                  TO* __restrict__ out) {
+  using R = typename Raw<TO>::type;
+  __shared__ float dec[256];
+  for (int u = threadIdx.x; u < 256; u += kRowThreads) {
+    if constexpr (E4M3) {
+      __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(u), __NV_E4M3);
+      dec[u] = __half2float(__half(hr));
+    } else {
+      dec[u] = __fmul_rn(__fdiv_rn(static_cast<float>(u - 128), 127.0f), 448.0f);
+    }
+  }
+  __syncthreads();
+  const int64_t n = rows * cols;
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * kRowThreads;
+  if (vec) {
+    constexpr int OV = static_cast<int>(sizeof(R));  // 16-byte output vectors per 16 codes
+    const int64_t cpr = cols / 16;
+    for (int64_t i = tid; i < n / 16; i += stride) {
+      const uint4 in = __ldcs(reinterpret_cast<const uint4*>(q) + i);
+      const float s = __ldg(scales + i / cpr);
+      const uint32_t w[4] = {in.x, in.y, in.z, in.w};
+      uint32_t o[4 * OV];  // the 16 outputs as 32-bit words, element k in the low bits first
+#pragma unroll
+      for (int k = 0; k < 16; ++k) {
+        const uint32_t r = to_raw<TO>(__fdiv_rn(dec[(w[k >> 2] >> (8 * (k & 3))) & 0xffu], s));
+        if constexpr (sizeof(R) == 2) {
+          if (k & 1) o[k >> 1] |= r << 16;
+          else o[k >> 1] = r;
+        } else {
+          o[k] = r;
+        }
+      }
+      uint4* dst = reinterpret_cast<uint4*>(out) + i * OV;
+#pragma unroll
+      for (int v = 0; v < OV; ++v) __stcs(dst + v, make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]));
+    }
+    return;
+  }
+  for (int64_t i = tid; i < n; i += stride) out[i] = Ty<TO>::from_f(__fdiv_rn(dec[q[i]], __ldg(scales + i / cols)));
+}
+
+// ---- decode ----------------------------------------------------------------
+constexpr int kDecThreads = 512;
+
+// out = RN_out( dec(u) / s ), dec(u) = RN(RN(float(u - 128) / 127) * 448) for
+// the reference codec (triton_ops/kernels/fp8_quantize.py:305-312) or the
+// e4m3 value of u. Only 256 outputs exist per call, so each CTA builds them
+// in shared memory and the stream becomes a table lookup.
 template <typename TO, bool E4M3>
 __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __restrict__ q, int64_t n, bool vec,
                                                              const float* __restrict__ scale, TO* __restrict__ out) {
@@ -830,10 +906,11 @@ int rows_grid(int64_t work) { return grid_for(std::max<int64_t>(work, 1), kRowTh
 
 cudaError_t row_scales_launch(const void* x, int64_t rows, int64_t cols, int x_dtype, float* scales, cudaStream_t st) {
   const int grid = rows_grid(rows * 32);
+  const bool vec = al16(x) && cols % 16 == 0;  // every row starts on a 16-byte boundary
   switch (x_dtype) {
-    case F16: row_scales_kernel<__half><<<grid, kRowThreads, 0, st>>>(static_cast<const __half*>(x), rows, cols, scales); break;
-    case BF16: row_scales_kernel<__nv_bfloat16><<<grid, kRowThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, scales); break;
-    default: row_scales_kernel<float><<<grid, kRowThreads, 0, st>>>(static_cast<const float*>(x), rows, cols, scales); break;
+    case F16: row_scales_kernel<__half><<<grid, kRowThreads, 0, st>>>(static_cast<const __half*>(x), rows, cols, vec, scales); break;
+    case BF16: row_scales_kernel<__nv_bfloat16><<<grid, kRowThreads, 0, st>>>(static_cast<const __nv_bfloat16*>(x), rows, cols, vec, scales); break;
+    default: row_scales_kernel<float><<<grid, kRowThreads, 0, st>>>(static_cast<const float*>(x), rows, cols, vec, scales); break;
   }
   note_launch();
   return cudaGetLastError();
@@ -842,9 +919,10 @@ cudaError_t row_scales_launch(const void* x, int64_t rows, int64_t cols, int x_d
 template <typename T>
 static cudaError_t enc_rows_t(const void* x, int64_t rows, int64_t cols, const float* scales, void* out, bool e4m3,
                               cudaStream_t st) {
-  const int grid = rows_grid(rows * cols);
-  if (e4m3) encode_rows_kernel<T, true><<<grid, kRowThreads, 0, st>>>(static_cast<const T*>(x), rows, cols, scales, static_cast<uint8_t*>(out));
-  else encode_rows_kernel<T, false><<<grid, kRowThreads, 0, st>>>(static_cast<const T*>(x), rows, cols, scales, static_cast<uint8_t*>(out));
+  const bool vec = al16(x) && al16(out) && cols % 16 == 0;
+  const int grid = rows_grid(vec ? rows * cols / 16 : rows * cols);
+  if (e4m3) encode_rows_kernel<T, true><<<grid, kRowThreads, 0, st>>>(static_cast<const T*>(x), rows, cols, vec, scales, static_cast<uint8_t*>(out));
+  else encode_rows_kernel<T, false><<<grid, kRowThreads, 0, st>>>(static_cast<const T*>(x), rows, cols, vec, scales, static_cast<uint8_t*>(out));
   note_launch();
   return cudaGetLastError();
 }
@@ -862,9 +940,10 @@ cudaError_t encode_rows_launch(const void* x, int64_t rows, int64_t cols, int x_
 template <typename TO>
 static cudaError_t dec_rows_t(const void* q, int64_t rows, int64_t cols, bool e4m3, const float* scales, void* out,
                               cudaStream_t st) {
-  const int grid = rows_grid(rows * cols);
-  if (e4m3) decode_rows_kernel<TO, true><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, scales, static_cast<TO*>(out));
-  else decode_rows_kernel<TO, false><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, scales, static_cast<TO*>(out));
+  const bool vec = al16(q) && al16(out) && cols % 16 == 0;
+  const int grid = rows_grid(vec ? rows * cols / 16 : rows * cols);
+  if (e4m3) decode_rows_kernel<TO, true><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, vec, scales, static_cast<TO*>(out));
+  else decode_rows_kernel<TO, false><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, vec, scales, static_cast<TO*>(out));
   note_launch();
   return cudaGetLastError();
 }
