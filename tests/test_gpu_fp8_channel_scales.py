@@ -88,7 +88,7 @@ def test_gemm_with_token_and_channel_scales(cuda, M, code):
 
 
 @pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
-@pytest.mark.parametrize("rows,cols", [(1, 16), (3, 48), (37, 1040), (16, 4096)])
+@pytest.mark.parametrize("rows,cols", [(1, 16), (3, 48), (37, 1040), (16, 4096), (3, 8208)])
 def test_per_row_vector_and_scalar_paths(cuda, dt, rows, cols):
     """Rows of whole 16-element chunks on 16-byte boundaries take the vectorised per-row kernels;
     the same values one element off a 16-byte boundary take the element-wise ones. Both equal the

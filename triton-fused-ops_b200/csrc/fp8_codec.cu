@@ -588,6 +588,64 @@ __global__ void __launch_bounds__(kRowThreads) decode_rows_kernel(const uint8_t*
   for (int64_t i = tid; i < n; i += stride) out[i] = Ty<TO>::from_f(__fdiv_rn(dec[q[i]], __ldg(scales + i / cols)));
 }
 
+// Rows of at least kLutRowCols codes (VEC conditions as above): one CTA per
+// row at a time builds that row's 256 outputs in shared memory (one division
+// per code value instead of one per element; the same rounded values), then
+// streams the row as table lookups.
+constexpr int64_t kLutRowCols = 4096;
+
+template <typename TO, bool E4M3>
+__global__ void __launch_bounds__(kRowThreads) decode_rows_lut_kernel(const uint8_t* __restrict__ q, int64_t rows,
+                                                                      int64_t cols, const float* __restrict__ scales,
+                                                                      TO* __restrict__ out) {
+  static_assert(kRowThreads == 256, "one thread per code value");
+  using R = typename Raw<TO>::type;
+  constexpr int OV = static_cast<int>(sizeof(R));  // 16-byte output vectors per 16 codes
+  __shared__ R lut[256];
+  float d;  // this thread's code value, decoded
+  if constexpr (E4M3) {
+    __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(threadIdx.x), __NV_E4M3);
+    d = __half2float(__half(hr));
+  } else {
+    d = __fmul_rn(__fdiv_rn(static_cast<float>(static_cast<int>(threadIdx.x) - 128), 127.0f), 448.0f);
+  }
+  const int64_t cpr = cols / 16;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float s = __ldg(scales + r);
+    __syncthreads();  // the previous row's lookups are done before the table changes
+    lut[threadIdx.x] = static_cast<R>(to_raw<TO>(__fdiv_rn(d, s)));
+    __syncthreads();
+    const uint4* qr = reinterpret_cast<const uint4*>(q + r * cols);
+    uint4* orow = reinterpret_cast<uint4*>(out + r * cols);
+    for (int64_t c = threadIdx.x; c < cpr; c += 2 * kRowThreads) {
+      uint4 in[2];
+      in[0] = __ldcs(qr + c);
+      if (c + kRowThreads < cpr) in[1] = __ldcs(qr + c + kRowThreads);
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int64_t cc = c + u * kRowThreads;
+        if (cc < cpr) {
+          const uint32_t w[4] = {in[u].x, in[u].y, in[u].z, in[u].w};
+          uint32_t o[4 * OV];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) {
+            const uint32_t v = lut[(w[k >> 2] >> (8 * (k & 3))) & 0xffu];
+            if constexpr (sizeof(R) == 2) {
+              if (k & 1) o[k >> 1] |= v << 16;
+              else o[k >> 1] = v;
+            } else {
+              o[k] = v;
+            }
+          }
+#pragma unroll
+          for (int v = 0; v < OV; ++v)
+            __stcs(orow + cc * OV + v, make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]));
+        }
+      }
+    }
+  }
+}
+
 // ---- decode ----------------------------------------------------------------
 constexpr int kDecThreads = 512;
 
@@ -941,6 +999,13 @@ template <typename TO>
 static cudaError_t dec_rows_t(const void* q, int64_t rows, int64_t cols, bool e4m3, const float* scales, void* out,
                               cudaStream_t st) {
   const bool vec = al16(q) && al16(out) && cols % 16 == 0;
+  if (vec && cols >= kLutRowCols) {
+    const int grid = static_cast<int>(std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * 8));
+    if (e4m3) decode_rows_lut_kernel<TO, true><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, scales, static_cast<TO*>(out));
+    else decode_rows_lut_kernel<TO, false><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, scales, static_cast<TO*>(out));
+    note_launch();
+    return cudaGetLastError();
+  }
   const int grid = rows_grid(vec ? rows * cols / 16 : rows * cols);
   if (e4m3) decode_rows_kernel<TO, true><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, vec, scales, static_cast<TO*>(out));
   else decode_rows_kernel<TO, false><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, vec, scales, static_cast<TO*>(out));
