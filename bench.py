@@ -391,6 +391,24 @@ def components(peaks, flush_buf):
     out["fp8linear_16x4096x4096"] = entry(us, err, us_call, flops=2.0 * 16 * 4096 * 4096)
     del xd, lin
 
+    # per-token scales at [4096, 4096] fp16: the row scales, then quantize and
+    # dequantize with one scale per row (reference codec)
+    xr = _copies(lambda: torch.randn(4096, 4096, device=dev, generator=g).half(), 4096 * 4096 * 2)
+    per_row = triton_ops.FP8Format.compute_scale_per_channel
+    rs = [per_row(x, dim=-1).float() for x in xr]
+    us, err = time_graph([lambda x=x: per_row(x, dim=-1) for x in xr])
+    us_call = 1e3 * time_events(lambda: per_row(xr[0], dim=-1), 30, flush_buf)
+    out["fp8_row_scales_4096x4096"] = entry(us, err, us_call, nbytes=2 * 4096 * 4096)
+    us, err = time_graph([lambda x=x, s=s: triton_ops.quantize_fp8(x, s) for x, s in zip(xr, rs)])
+    us_call = 1e3 * time_events(lambda: triton_ops.quantize_fp8(xr[0], rs[0]), 30, flush_buf)
+    out["fp8_quantize_rows_4096x4096"] = entry(us, err, us_call, nbytes=3 * 4096 * 4096)
+    qr = [triton_ops.quantize_fp8(x, s)[0] for x, s in zip(xr, rs)]
+    del xr
+    us, err = time_graph([lambda q=q, s=s: triton_ops.dequantize_fp8(q, s) for q, s in zip(qr, rs)])
+    us_call = 1e3 * time_events(lambda: triton_ops.dequantize_fp8(qr[0], rs[0]), 30, flush_buf)
+    out["fp8_dequantize_rows_4096x4096"] = entry(us, err, us_call, nbytes=3 * 4096 * 4096)
+    del qr, rs
+
     # FP8 GEMM over M, N = K = 4096: reference codec (int8 tensor cores), e4m3
     # (fp8 tensor cores), and the library fp8 GEMM (torch._scaled_mm) on the
     # same e4m3 operands as a comparator
