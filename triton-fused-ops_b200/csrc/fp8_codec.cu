@@ -589,9 +589,10 @@ __global__ void __launch_bounds__(kRowThreads) decode_rows_kernel(const uint8_t*
 }
 
 // Rows of at least kLutRowCols codes (VEC conditions as above): one CTA per
-// row at a time builds that row's 256 outputs in shared memory (one division
-// per code value instead of one per element; the same rounded values), then
-// streams the row as table lookups.
+// pair of rows at a time builds the two rows' 256 outputs each in shared
+// memory (one division per code value instead of one per element; the same
+// rounded values), then streams both rows, contiguous in memory, as table
+// lookups with four 16-byte code vectors in flight per thread.
 constexpr int64_t kLutRowCols = 4096;
 
 template <typename TO, bool E4M3>
@@ -601,7 +602,8 @@ __global__ void __launch_bounds__(kRowThreads) decode_rows_lut_kernel(const uint
   static_assert(kRowThreads == 256, "one thread per code value");
   using R = typename Raw<TO>::type;
   constexpr int OV = static_cast<int>(sizeof(R));  // 16-byte output vectors per 16 codes
-  __shared__ R lut[256];
+  constexpr int U = 4;                              // code vectors in flight per thread
+  __shared__ R lut[2][256];
   float d;  // this thread's code value, decoded
   if constexpr (E4M3) {
     __half_raw hr = __nv_cvt_fp8_to_halfraw(static_cast<__nv_fp8_storage_t>(threadIdx.x), __NV_E4M3);
@@ -610,26 +612,32 @@ __global__ void __launch_bounds__(kRowThreads) decode_rows_lut_kernel(const uint
     d = __fmul_rn(__fdiv_rn(static_cast<float>(static_cast<int>(threadIdx.x) - 128), 127.0f), 448.0f);
   }
   const int64_t cpr = cols / 16;
-  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-    const float s = __ldg(scales + r);
-    __syncthreads();  // the previous row's lookups are done before the table changes
-    lut[threadIdx.x] = static_cast<R>(to_raw<TO>(__fdiv_rn(d, s)));
+  for (int64_t r0 = 2 * static_cast<int64_t>(blockIdx.x); r0 < rows; r0 += 2 * static_cast<int64_t>(gridDim.x)) {
+    const bool two = r0 + 1 < rows;
+    const float s0 = __ldg(scales + r0);
+    const float s1 = two ? __ldg(scales + r0 + 1) : 1.0f;
+    __syncthreads();  // the previous pair's lookups are done before the tables change
+    lut[0][threadIdx.x] = static_cast<R>(to_raw<TO>(__fdiv_rn(d, s0)));
+    lut[1][threadIdx.x] = static_cast<R>(to_raw<TO>(__fdiv_rn(d, s1)));
     __syncthreads();
-    const uint4* qr = reinterpret_cast<const uint4*>(q + r * cols);
-    uint4* orow = reinterpret_cast<uint4*>(out + r * cols);
-    for (int64_t c = threadIdx.x; c < cpr; c += 2 * kRowThreads) {
-      uint4 in[2];
-      in[0] = __ldcs(qr + c);
-      if (c + kRowThreads < cpr) in[1] = __ldcs(qr + c + kRowThreads);
+    const int64_t nch = (two ? 2 : 1) * cpr;  // chunks of the pair; chunk k is in row r0 + (k >= cpr)
+    const uint4* qr = reinterpret_cast<const uint4*>(q + r0 * cols);
+    uint4* orow = reinterpret_cast<uint4*>(out + r0 * cols);
+    for (int64_t c = threadIdx.x; c < nch; c += U * kRowThreads) {
+      uint4 in[U];
 #pragma unroll
-      for (int u = 0; u < 2; ++u) {
+      for (int u = 0; u < U; ++u)
+        if (c + u * kRowThreads < nch) in[u] = __ldcs(qr + c + u * kRowThreads);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
         const int64_t cc = c + u * kRowThreads;
-        if (cc < cpr) {
+        if (cc < nch) {
+          const R* tab = lut[cc >= cpr ? 1 : 0];
           const uint32_t w[4] = {in[u].x, in[u].y, in[u].z, in[u].w};
           uint32_t o[4 * OV];
 #pragma unroll
           for (int k = 0; k < 16; ++k) {
-            const uint32_t v = lut[(w[k >> 2] >> (8 * (k & 3))) & 0xffu];
+            const uint32_t v = tab[(w[k >> 2] >> (8 * (k & 3))) & 0xffu];
             if constexpr (sizeof(R) == 2) {
               if (k & 1) o[k >> 1] |= v << 16;
               else o[k >> 1] = v;
@@ -1000,7 +1008,7 @@ static cudaError_t dec_rows_t(const void* q, int64_t rows, int64_t cols, bool e4
                               cudaStream_t st) {
   const bool vec = al16(q) && al16(out) && cols % 16 == 0;
   if (vec && cols >= kLutRowCols) {
-    const int grid = static_cast<int>(std::min<int64_t>(rows, static_cast<int64_t>(num_sms()) * 8));
+    const int grid = static_cast<int>(std::min<int64_t>((rows + 1) / 2, static_cast<int64_t>(num_sms()) * 8));
     if (e4m3) decode_rows_lut_kernel<TO, true><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, scales, static_cast<TO*>(out));
     else decode_rows_lut_kernel<TO, false><<<grid, kRowThreads, 0, st>>>(static_cast<const uint8_t*>(q), rows, cols, scales, static_cast<TO*>(out));
     note_launch();
