@@ -75,7 +75,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "50"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
         time.sleep(0.3)
@@ -153,7 +153,7 @@ def max_over_ranks(v: float, world: int) -> float:
 
 
 def rope_tables(seq_len: int, head_dim: int, device):
-    """HF-style cos/sin [seq_len, head_dim] = cat(f, f), f = pos * 10000^(-2i/head_dim), as fp16."""
+    """HF-style cos/sin [seq_len, head_dim] = cat(f, f), f = pos * 10000^(-2i/head_dim), as fp16 on `device`."""
     import torch
 
     inv = 1.0 / (10000.0 ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
@@ -188,76 +188,186 @@ def time_events(fn, reps, flush_buf=None):
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline: numpy restatement of the reference's PyTorch path
+# CPU baseline: the reference's PyTorch CPU path
 # ---------------------------------------------------------------------------
-class CpuPath:
-    """The reference's CPU path restated in numpy: fp32 RMSNorm+RoPE math, fp32 gated-MLP matmuls."""
-
-    def __init__(self, sample_rows: int):
-        import numpy as np
-
-        from oracle import tfo_oracle as O
-
-        self.O = O
-        self.rows = sample_rows
-        rng = np.random.default_rng(0)
-        self.x = O.round_to(rng.standard_normal((1, sample_rows, H), dtype=np.float32), "f16")
-        self.w = O.round_to((1 + 0.1 * rng.standard_normal(H)).astype(np.float32), "f16")
-        cos, sin = O.rope_tables(sample_rows, D)
-        self.cos, self.sin = O.round_to(cos, "f16"), O.round_to(sin, "f16")
-        self.wg = O.round_to((0.02 * rng.standard_normal((I, H))).astype(np.float32), "f16")
-        self.wu = O.round_to((0.02 * rng.standard_normal((I, H))).astype(np.float32), "f16")
-
-    def step(self):
-        y = self.O.rmsnorm_rope(self.x, self.w, self.cos, self.sin, 1e-6, "f16")
-        return self.O.gated_mlp_f32(y, self.wg, self.wu, "silu", "f16")
+# The reference's own CPU implementation of these ops is its PyTorch oracle
+# functions (rmsnorm_rope.py:356-383, fp8_quantize.py:258-312,
+# fp8_gemm.py:190-225, gated_mlp.py:221-251). This package carries the same
+# torch expressions as ``triton_ops.kernels.*.*_reference`` (the reference's
+# tests import them); they run here on CPU tensors with every host thread.
+CPU_SAMPLE_ROWS = 1024  # token rows per CPU step (positions 0..1023 of one sequence)
 
 
 def cpu_cores():
     return len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
 
 
-def cpu_baseline(sample_rows: int = 64, max_seconds: float = 15.0):
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or "unknown"
+
+
+def cpu_threads():
+    import torch
+
+    torch.set_num_threads(cpu_cores())
+    return torch.get_num_threads()
+
+
+class CpuPath:
+    """The prefill step on CPU_SAMPLE_ROWS token rows through the reference's
+    PyTorch functions: RMSNorm+RoPE (fp32 math, fp16 result) then the gated MLP
+    (fp32 projections of the fp16 operands, SiLU, fp16 result)."""
+
+    def __init__(self, rows: int = CPU_SAMPLE_ROWS):
+        import torch
+
+        from triton_ops.kernels.gated_mlp import gated_mlp_reference
+        from triton_ops.kernels.rmsnorm_rope import fused_rmsnorm_rope_reference
+
+        self.rows = rows
+        self.rms, self.mlp = fused_rmsnorm_rope_reference, gated_mlp_reference
+        g = torch.Generator().manual_seed(0)
+        self.x = torch.randn(1, rows, H, generator=g).half()
+        self.w = (1 + 0.1 * torch.randn(H, generator=g)).half()
+        self.cos, self.sin = rope_tables(rows, D, "cpu")
+        self.wg = (0.02 * torch.randn(I, H, generator=g)).half()
+        self.wu = (0.02 * torch.randn(I, H, generator=g)).half()
+
+    def step(self):
+        y = self.rms(self.x, self.w, self.cos, self.sin, 1e-6)
+        return self.mlp(y, self.wg, self.wu, "silu")
+
+
+def cpu_sample_text(rows, n, dt):
+    return (f"{rows} of {ROWS} token rows per step (positions 0..{rows - 1}): the reference's PyTorch "
+            f"fused_rmsnorm_rope_reference -> gated_mlp_reference (fp32 math) on CPU tensors, "
+            f"{n} steps of {dt * 1e3:.1f} ms measured")
+
+
+def cpu_baseline(max_seconds: float = 12.0):
     """Times the CPU path on a bounded row sample (reported beside the GPU number)."""
-    path = CpuPath(sample_rows)
-    path.step()  # warm-up
-    t0 = time.perf_counter()
-    n = 0
-    while n < 3 or (time.perf_counter() - t0 < max_seconds and n < 50):
+    threads = cpu_threads()
+    path = CpuPath()
+    path.step()  # warm-up (thread pool, first-touch)
+    times = []
+    t_end = time.perf_counter() + max_seconds
+    while len(times) < 3 or (time.perf_counter() < t_end and len(times) < 20):
+        t0 = time.perf_counter()
         path.step()
-        n += 1
-    dt = (time.perf_counter() - t0) / n
-    return {"value": sample_rows * FLOPS_PER_ROW / dt / 1e12, "unit": "TFLOP/s", "cores": cpu_cores(),
-            "kind": "port",
-            "sample": f"{sample_rows} of {ROWS} token rows per step (numpy fp32 RMSNorm+RoPE and gated-MLP "
-                      f"matmuls), {n} steps of {dt * 1e3:.1f} ms"}
+        times.append(time.perf_counter() - t0)
+    dt = statistics.median(times)
+    return {"value": path.rows * FLOPS_PER_ROW / dt / 1e12, "unit": "TFLOP/s", "cores": threads,
+            "cpu_model": cpu_model(), "kind": "port", "ms_per_step": dt * 1e3,
+            "sample": cpu_sample_text(path.rows, len(times), dt)}
+
+
+def time_cpu(fn, max_seconds: float = 3.0, max_reps: int = 5):
+    """Median seconds of fn() on the CPU after one warm-up call (bounded by max_seconds)."""
+    fn()
+    times = []
+    t_end = time.perf_counter() + max_seconds
+    while not times or (time.perf_counter() < t_end and len(times) < max_reps):
+        t0 = time.perf_counter()
+        fn()
+        times.append(time.perf_counter() - t0)
+    return statistics.median(times)
+
+
+def cpu_components():
+    """The reference's PyTorch CPU functions at every configuration's shape.
+
+    Returns {component name: microseconds per call}; names match the GPU
+    `components` entries they sit beside.
+    """
+    import torch
+
+    from triton_ops.kernels.fp8_gemm import fp8_gemm_reference
+    from triton_ops.kernels.fp8_quantize import fp8_dequantize_reference, fp8_quantize_reference
+    from triton_ops.kernels.gated_mlp import gated_mlp_reference
+    from triton_ops.kernels.rmsnorm_rope import fused_rmsnorm_rope_reference
+
+    cpu_threads()
+    g = torch.Generator().manual_seed(7)
+    out = {}
+    # config 1: [2, 128, 4096], fp32 on the CPU
+    x = torch.randn(2, 128, 4096, generator=g)
+    w = 1 + 0.1 * torch.randn(4096, generator=g)
+    cos, sin = rope_tables(128, 64, "cpu")
+    cos, sin = cos.float(), sin.float()
+    out["rmsnorm_rope_2x128x4096"] = 1e6 * time_cpu(lambda: fused_rmsnorm_rope_reference(x, w, cos, sin, 1e-6))
+    # config 2: [4096, 4096] fp16 with 0.1% outliers of +-200, dynamic scale
+    t = torch.randn(4096, 4096, generator=g).half()
+    idx = torch.randperm(t.numel(), generator=g)[: t.numel() // 1000]
+    t.view(-1)[idx] = 200.0 * torch.sign(torch.randn(idx.numel(), generator=g)).half()
+    out["fp8_quantize_4096x4096"] = 1e6 * time_cpu(lambda: fp8_quantize_reference(t))
+    q, s = fp8_quantize_reference(t)
+    out["fp8_dequantize_4096x4096"] = 1e6 * time_cpu(lambda: fp8_dequantize_reference(q, s))
+    # config 3: codes A [M, 4096], B [4096, 4096], fp16 out
+    qb, sb = fp8_quantize_reference(torch.randn(4096, 4096, generator=g).half())
+    gemm = {}
+    for M in (16, 128, 1024, 4096, 8192):
+        qa, sa = fp8_quantize_reference(torch.randn(M, 4096, generator=g).half())
+        gemm[str(M)] = 1e6 * time_cpu(lambda: fp8_gemm_reference(qa, qb, sa, sb), max_reps=3)
+    out["fp8_gemm_Mx4096x4096"] = gemm
+    # config 4: x [2, 1024, 4096] fp16, W [11264, 4096] fp16
+    xm = torch.randn(2, 1024, 4096, generator=g).half()
+    wg = (0.02 * torch.randn(11264, 4096, generator=g)).half()
+    wu = (0.02 * torch.randn(11264, 4096, generator=g)).half()
+    for act in ("silu", "gelu", "gelu_tanh"):
+        out[f"gated_mlp_2x1024x4096_{act}"] = 1e6 * time_cpu(lambda: gated_mlp_reference(xm, wg, wu, act),
+                                                             max_reps=3)
+    return out
+
+
+def bench_config(world: int) -> dict:
+    """The workload description both arms print (identical for the same N)."""
+    return {
+        "workload": "prefill RMSNorm+RoPE -> gated MLP (SiLU), x [8, 8192, 4096] fp16 row-sharded, "
+                    "W_gate/W_up [11264, 4096] fp16, head_dim 64",
+        "rows": ROWS, "rows_per_rank": -(-ROWS // world), "hidden": H, "intermediate": I, "head_dim": D,
+        "parallelism": f"rows{world}" if world > 1 else "single",
+        "l2": "inputs larger than L2: two alternating x slabs; per-step traffic > 4x L2",
+    }
 
 
 def run_reference(args):
-    """The reference's CPU implementation of the path (numpy restatement), rank 0 only."""
+    """The reference's CPU implementation of the path, rank 0 only.
+
+    Each step runs the prefill step's ops on CPU_SAMPLE_ROWS token rows (a
+    bounded sample of the 65,536-row slab) and is timed as it runs; `value` is
+    the measured rate (tensor flops of the sample / step time) and
+    `ms_per_step` the measured time of one sample step.
+    """
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", str(args.gpus)))
     if rank != 0:
         return 0
-    rows = 64
-    path = CpuPath(rows)
+    threads = cpu_threads()
+    path = CpuPath()
     for _ in range(args.warmup):
         path.step()
     t0 = time.perf_counter()
     for _ in range(args.steps):
         path.step()
     dt = (time.perf_counter() - t0) / args.steps
-    value = rows * FLOPS_PER_ROW / dt / 1e12
-    sample = f"{rows} of {ROWS} token rows per step (numpy fp32 RMSNorm+RoPE and gated-MLP matmuls)"
+    value = path.rows * FLOPS_PER_ROW / dt / 1e12
+    sample = cpu_sample_text(path.rows, args.steps, dt)
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ROWS * FLOPS_PER_ROW / (value * 1e12) * 1e3,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16 (fp32 math on CPU)",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(1,0.1) norm weight)",
-            "config": {"workload": "prefill RMSNorm+RoPE -> gated MLP (SiLU), x [8, 8192, 4096] fp16 row-sharded, "
-                                   "W_gate/W_up [11264, 4096] fp16, head_dim 64",
-                       "rows": ROWS, "hidden": H, "intermediate": I, "head_dim": D},
+            "config": bench_config(world),
             "impl": "reference",
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
-                             "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "cpu_model": cpu_model(),
+                             "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line))
     return 0
@@ -444,10 +554,43 @@ def components(peaks, flush_buf):
         except Exception as exc:  # noqa: BLE001 - comparator only
             lib8[str(M)] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
         del qa, qa8, a_f
+    del bs, bs8, bs8_nk
+    # FP8 tensor peak measured in this run: the library fp8 GEMM (cuBLASLt
+    # through torch._scaled_mm, e4m3, fp32 accumulate) at 8192^3, best of 10
+    # back-to-back launches (a burst, like the bf16 peak); 2 x the measured
+    # bf16 burst is reported beside it
+    fp8_peak = None
+    try:
+        pa = torch.randn(8192, 8192, device=dev, generator=g).to(torch.float8_e4m3fn)
+        pb = torch.randn(8192, 8192, device=dev, generator=g).to(torch.float8_e4m3fn)
+        one = torch.ones((), device=dev)
+        best = min(time_events(lambda: torch._scaled_mm(pa, pb.t(), one, one, out_dtype=torch.bfloat16), 1)
+                   for _ in range(10))
+        fp8_peak = 2.0 * 8192**3 / (best / 1e3) / 1e12
+        del pa, pb
+    except Exception as exc:  # noqa: BLE001 - reported as missing
+        out["fp8_peak_error"] = f"{type(exc).__name__}: {exc}"[:200]
+    out["fp8_tensor_peak"] = {"TFLOP/s": fp8_peak, "how": "torch._scaled_mm e4m3 8192^3 -> bf16, best of 10, "
+                                                          "CUDA events, in this run",
+                              "two_x_bf16_burst": 2 * peaks["bf16_tflops"]}
+    for table in (gemm, gemm8):
+        for m, e in table.items():
+            M = int(m)
+            if e.get("us") is None:
+                continue
+            if M <= 128:  # below the ridge: bound by the operand bytes
+                nbytes = M * 4096 + 4096 * 4096 + 2 * M * 4096
+                ach = nbytes / e["us"] / 1e3
+                e["roofline"] = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                                 "algorithmic_bytes": nbytes, "peak_source": f"{peaks['source']} hbm_gbs"}
+            elif fp8_peak:
+                e["roofline"] = {"bound": "tensor", "achieved": e["TFLOP/s"], "peak": fp8_peak, "unit": "TFLOP/s",
+                                 "frac": e["TFLOP/s"] / fp8_peak,
+                                 "peak_source": "fp8 library GEMM measured in this run (fp8_tensor_peak)",
+                                 "frac_of_2x_bf16_burst": e["TFLOP/s"] / (2 * peaks["bf16_tflops"])}
     out["fp8_gemm_Mx4096x4096"] = gemm
     out["fp8_gemm_e4m3_Mx4096x4096"] = gemm8
     out["library_scaled_mm_e4m3_Mx4096x4096"] = lib8
-    del bs, bs8, bs8_nk
 
     # fused RMSNorm+RoPE -> 8-bit codes at the prefill shape [8, 8192, 4096] fp16,
     # dynamic and given scale, and the two ops run separately; GB/s counts the
@@ -483,7 +626,7 @@ def components(peaks, flush_buf):
     wg = (0.02 * torch.randn(11264, 4096, device=dev, generator=g)).half()
     wu = (0.02 * torch.randn(11264, 4096, device=dev, generator=g)).half()
     fl = 4.0 * 2048 * 11264 * 4096
-    for act in ("silu", "gelu_tanh"):
+    for act in ("silu", "gelu", "gelu_tanh"):
         us, err = time_graph([lambda x=x: triton_ops.fused_gated_mlp(x, wg, wu, act) for x in xm], reps=10)
         us_call = 1e3 * time_events(lambda: triton_ops.fused_gated_mlp(xm[0], wg, wu, act), 20, flush_buf)
         out[f"gated_mlp_2x1024x4096_{act}"] = entry(us, err, us_call, flops=fl, peak=peaks["bf16_tflops"])
@@ -499,6 +642,24 @@ def components(peaks, flush_buf):
     mq["unfused_given_scale"] = entry(us, err, None, flops=fl, peak=peaks["bf16_tflops"])
     out["gated_mlp_quantize_2x1024x4096_silu"] = mq
     return out
+
+
+def add_cpu_numbers(comps, cpu, threads):
+    """Puts each CPU time beside the GPU component of the same name."""
+    kind = f"port: the reference's PyTorch function on CPU tensors, {threads} threads"
+    for name, v in cpu.items():
+        target = comps.get(name)
+        if target is None:
+            continue
+        pairs = v.items() if isinstance(v, dict) else [(None, v)]
+        for key, cpu_us in pairs:
+            e = target.get(key) if key is not None else target
+            if not isinstance(e, dict):
+                continue
+            e["cpu_us"] = cpu_us
+            e["cpu_kind"] = kind + (" (fp32 input)" if name == "rmsnorm_rope_2x128x4096" else "")
+            if e.get("us"):
+                e["gpu_speedup_vs_cpu"] = cpu_us / e["us"]
 
 
 def read_traffic():
@@ -685,6 +846,8 @@ def run_ours(args):
             comps = components(peaks, flush)
         if not args.no_cpu_baseline:
             cpu = cpu_baseline()
+            if comps is not None:
+                add_cpu_numbers(comps, cpu_components(), cpu["cores"])
 
     if rank == 0:
         mlp_tflops = mlp_flops_launch / (mlp_ms / 1e3) / 1e12
@@ -703,13 +866,7 @@ def run_ours(args):
             "vs_baseline": None,
             "dtype": "f16 (fp32 accumulate)",
             "data": "synthetic (seeded N(0,1) activations, N(0,0.02) weights, N(1,0.1) norm weight)",
-            "config": {
-                "workload": "prefill RMSNorm+RoPE -> gated MLP (SiLU), x [8, 8192, 4096] fp16 row-sharded, "
-                            "W_gate/W_up [11264, 4096] fp16, head_dim 64",
-                "rows": ROWS, "rows_per_rank": rows, "hidden": H, "intermediate": I, "head_dim": D,
-                "parallelism": f"rows{world}" if world > 1 else "single",
-                "l2": "inputs larger than L2: two alternating x slabs; per-step traffic > 4x L2",
-            },
+            "config": bench_config(world),
             "roofline": {
                 "bound": "tensor", "kernel": "gated_mlp (tcgen05 kind::f16)",
                 "achieved": mlp_tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",

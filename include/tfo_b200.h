@@ -149,8 +149,10 @@ TFO_API int tfo_fp8_quantize(const void* x, int64_t numel, int x_dtype, const fl
  * every GPU that loads the library keeps until the process exits. Limit: a
  * call may need at most 4096 partial slots (one per amax block, at most
  * 2 x the SM count, i.e. 296 on a 148-SM B200); larger needs are rejected with
- * TFO_ERR_INVALID and an explanatory message. The first call on each device
- * looks up the scratch address, so make it before any stream capture. All
+ * TFO_ERR_INVALID and an explanatory message. The first call in each CUDA
+ * context (per device, and again after cudaDeviceReset or in another context
+ * made current through the driver API) looks up the scratch address in that
+ * context, so make it before any stream capture. All
  * calls share the scratch: calls that overlap on the GPU (different streams,
  * same device) race and must be serialised by the caller.
  * No counterpart in the reference; same results as tfo_fp8_quantize with a

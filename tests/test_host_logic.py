@@ -169,3 +169,27 @@ def test_validation_order_matches_reference_on_cpu():
     # device is checked before the activation name, as in the reference
     with pytest.raises(DeviceError):
         validate_gated_mlp_inputs(x, torch.randn(4, 8), torch.randn(4, 8), activation="invalid")
+
+
+def test_workspace_cache_is_bounded_and_clearable(monkeypatch):
+    """One buffer per (device, stream), grow-only, least recently used dropped past the cap."""
+    from triton_ops import _lib
+
+    handles = iter(range(1000, 2000))
+    current = {"h": next(handles)}
+    monkeypatch.setattr(_lib, "_raw_stream", lambda idx: current["h"])
+    monkeypatch.setattr(_lib, "_is_capturing", lambda: False)
+    _lib.clear_workspaces()
+    dev = torch.device("cpu", 0)
+    a = _lib.workspace(100, dev)
+    assert _lib.workspace(50, dev) is a  # same stream, fits: reused
+    b = _lib.workspace(1000, dev)
+    assert b is not a and b.numel() >= 1000  # grown
+    first = current["h"]
+    for _ in range(_lib._WS_MAX_ENTRIES + 3):  # a new stream per call
+        current["h"] = next(handles)
+        _lib.workspace(16, dev)
+    assert len(_lib._ws_cache) == _lib._WS_MAX_ENTRIES
+    assert (0, first) not in _lib._ws_cache  # the oldest stream's buffer was dropped
+    _lib.clear_workspaces()
+    assert len(_lib._ws_cache) == 0

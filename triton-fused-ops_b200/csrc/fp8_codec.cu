@@ -14,7 +14,9 @@
 //                         derives the scale in double, CTA 0 publishes it,
 //                         then encodes its share of the tensor.
 // The second read of x is served by L2 for tensors that fit in it.
-#include <atomic>
+#include <cuda.h>
+
+#include <mutex>
 #include <string>
 
 #include "capi_internal.h"
@@ -1043,25 +1045,67 @@ constexpr int kNoallocMaxPartials = 4096;
 static __device__ __align__(256) uint32_t g_noalloc_partials[kNoallocMaxPartials];
 
 namespace {
-// Device address of g_noalloc_partials per device. The array's name is only a
-// host-side stand-in in host code, so the address is looked up once per
-// device, with that device current, and passed to the kernels.
-std::atomic<uint32_t*> g_noalloc_ptr[64];
+// Device address of g_noalloc_partials, looked up with cudaGetSymbolAddress
+// (in host code the array's name is only a host-side stand-in) and cached per
+// CUDA context. The key is the context's unique id (cuCtxGetId), never reused
+// within a process: after cudaDeviceReset, or with another context made
+// current through the driver API, the id changes and the address is looked up
+// again instead of reusing one that belongs to a destroyed or other context.
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+struct NoallocSlot {
+  unsigned long long ctx_id;
+  uint32_t* ptr;
+};
+constexpr int kNoallocSlots = 64;
+NoallocSlot g_noalloc_slots[kNoallocSlots];
+int g_noalloc_next = 0;
+std::mutex g_noalloc_mu;
+
+bool current_context_id(unsigned long long* id) {
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_current = reinterpret_cast<CtxGetCurrentFn>(p);
+    p = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      get_id = reinterpret_cast<CtxGetIdFn>(p);
+  });
+  CUcontext ctx = nullptr;
+  if (get_current == nullptr || get_id == nullptr || get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+    return false;
+  return get_id(ctx, id) == CUDA_SUCCESS;
+}
 
 cudaError_t noalloc_scratch(uint32_t** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
-  uint32_t* p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
-  if (p == nullptr) {
-    void* addr = nullptr;
-    e = cudaGetSymbolAddress(&addr, g_noalloc_partials);
-    if (e != cudaSuccess) return e;
-    p = static_cast<uint32_t*>(addr);
-    g_noalloc_ptr[dev].store(p, std::memory_order_release);
+  unsigned long long id = 0;
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  const bool have_id = current_context_id(&id);
+  if (have_id) {
+    for (int i = 0; i < kNoallocSlots; ++i) {
+      if (g_noalloc_slots[i].ptr != nullptr && g_noalloc_slots[i].ctx_id == id) {
+        *out = g_noalloc_slots[i].ptr;
+        return cudaSuccess;
+      }
+    }
   }
-  *out = p;
+  // First call in this context (this also makes the runtime's context current
+  // when none was): look the address up with the device current.
+  void* addr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&addr, g_noalloc_partials);
+  if (e != cudaSuccess) return e;
+  if (have_id || current_context_id(&id)) {
+    g_noalloc_slots[g_noalloc_next] = NoallocSlot{id, static_cast<uint32_t*>(addr)};
+    g_noalloc_next = (g_noalloc_next + 1) % kNoallocSlots;
+  }
+  *out = static_cast<uint32_t*>(addr);
   return cudaSuccess;
 }
 }  // namespace

@@ -12,6 +12,7 @@ from __future__ import annotations
 import ctypes
 import os
 import threading
+from collections import OrderedDict
 from pathlib import Path
 
 import torch
@@ -211,10 +212,18 @@ def version() -> str:
 
 # One grow-only scratch buffer per (device, stream): calls on one stream run in
 # order, so each may reuse the buffer of the one before. (A fresh tensor from
-# torch's caching allocator costs ~2 us of host time per call.) While a CUDA
-# graph is being captured a fresh tensor is taken instead, so that no buffer
-# is shared between a graph's private pool and eager calls.
-_ws_cache: dict = {}
+# torch's caching allocator costs ~2 us of host time per call.) At most
+# _WS_MAX_ENTRIES (device, stream) buffers are kept, least recently used first
+# out, so a process that makes a stream per request does not keep one buffer
+# per stream it ever used; clear_workspaces() drops them all (for example after
+# destroying streams, since a new stream may receive a destroyed one's handle).
+# Dropping a buffer is safe while kernels that use it are in flight: the
+# caching allocator reuses its memory only in that stream's order.
+# While a CUDA graph is being captured a fresh tensor is taken instead, so that
+# no buffer is shared between a graph's private pool and eager calls.
+_WS_MAX_ENTRIES = 8
+_ws_cache: OrderedDict = OrderedDict()
+_ws_lock = threading.Lock()
 _is_capturing = getattr(torch.cuda, "is_current_stream_capturing", lambda: False)
 
 
@@ -225,8 +234,18 @@ def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
         return torch.empty(n, dtype=torch.uint8, device=device)
     idx = device.index if device.index is not None else torch.cuda.current_device()
     key = (idx, _raw_stream(idx) if _raw_stream is not None else torch.cuda.current_stream(idx).cuda_stream)
-    buf = _ws_cache.get(key)
-    if buf is None or buf.numel() < n:
-        buf = torch.empty(max(n, 2 * buf.numel() if buf is not None else n), dtype=torch.uint8, device=device)
-        _ws_cache[key] = buf
+    with _ws_lock:
+        buf = _ws_cache.get(key)
+        if buf is None or buf.numel() < n:
+            buf = torch.empty(max(n, 2 * buf.numel() if buf is not None else n), dtype=torch.uint8, device=device)
+            _ws_cache[key] = buf
+        _ws_cache.move_to_end(key)
+        while len(_ws_cache) > _WS_MAX_ENTRIES:
+            _ws_cache.popitem(last=False)
     return buf
+
+
+def clear_workspaces() -> None:
+    """Releases every cached scratch buffer (they return to torch's caching allocator)."""
+    with _ws_lock:
+        _ws_cache.clear()
