@@ -316,6 +316,15 @@ inline size_t vec_smem_bytes(int hidden, int row_bytes, int stages) {
 // cos/sin offsets) is the same for every j.
 // At most 12 warps with 16 vectors per lane (row kept in 64 registers), 16 otherwise.
 constexpr int warp_rows_max_warps(int vpl) { return vpl >= 16 ? 12 : 16; }
+// Per-warp raw cos/sin slot of the warp-per-row kernel: two halves of up to
+// kMaxHalfHead fp32 entries would be 1 KB; head_dim <= 64 tables use <= 256 B.
+constexpr int kCsRawBytes = 256;
+// Row buffers per warp: a warp's next row is in flight while it works on the
+// current one and the one after that while it finishes (with one buffer the
+// next load only started after the current row's first pass).
+constexpr int kWarpSlots = 2;
+constexpr int kWarpBarBytes = 32 * 8;  // up to 32 mbarriers (warps x slots)
+static_assert(16 * kWarpSlots <= 32, "barrier area");
 
 // MODE 0 stores the output rows; MODE 3 also writes one max |output value|
 // per CTA to q.parts_out (the amax partials of a dynamic-scale quantize of the
@@ -324,7 +333,7 @@ template <typename TX, typename TCS, bool FULLROT, int VPL, int MODE>
 __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope_warp_kernel(
     const TX* __restrict__ x, const void* __restrict__ w, const TCS* __restrict__ cosp, const TCS* __restrict__ sinp,
     TX* __restrict__ out, int64_t rows, int seq_len, int hidden, int head_dim, int rot_cols, int64_t cs_ss,
-    int64_t cs_sd, float eps, int w_dtype, int cs_stride, uint32_t* err, const RowQuantArgs q) {
+    int64_t cs_sd, float eps, int w_dtype, int cs_stride, bool cs_bulk, uint32_t* err, const RowQuantArgs q) {
   griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
   constexpr int E = Pack<TX>::E;
   constexpr bool kExactProducts = sizeof(TX) == 2 && sizeof(TCS) == 2;
@@ -337,15 +346,36 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
   const uint32_t row_bytes = static_cast<uint32_t>(hidden) * sizeof(TX);
 
   extern __shared__ __align__(128) uint8_t smem[];
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                // [W]
-  float* wsm = reinterpret_cast<float*>(smem + 16 * 8);              // [hidden]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem);                // [W][kWarpSlots]
+  float* wsm = reinterpret_cast<float*>(smem + kWarpBarBytes);       // [hidden]
   float* csm = wsm + hidden;                                         // [W][cs_stride]
-  uint8_t* ring = smem + ((16 * 8 + (static_cast<size_t>(hidden) + W * cs_stride) * 4 + 127) / 128) * 128;
+  uint8_t* ring = smem + ((kWarpBarBytes + (static_cast<size_t>(hidden) + W * cs_stride) * 4 + 127) / 128) * 128;
 
-  uint64_t* full = bars + warp;
   float* cs_buf = csm + warp * cs_stride;   // cos[half], sin[half], -sin[half]
-  uint8_t* slot = ring + static_cast<size_t>(warp) * row_bytes;
-  const uint4* rv = reinterpret_cast<const uint4*>(slot);
+  // kWarpSlots row buffers per warp (row k of the warp in buffer k % kWarpSlots,
+  // each with its own mbarrier): a buffer is refilled with row k + kWarpSlots
+  // as soon as row k has moved into registers.
+  // cs_bulk: the row's cos and sin halves (contiguous, 16-byte aligned) arrive
+  // with the row by bulk copy into the buffer's raw table slot, so a row never
+  // waits on global loads of its table entries
+  const uint32_t cs_half_bytes = static_cast<uint32_t>(half) * sizeof(TCS);
+  auto slot_of = [&](int b) { return ring + static_cast<size_t>(warp * kWarpSlots + b) * row_bytes; };
+  auto cs_raw_of = [&](int b) {
+    return reinterpret_cast<TCS*>(ring + static_cast<size_t>(W * kWarpSlots) * row_bytes +
+                                  static_cast<size_t>(warp * kWarpSlots + b) * kCsRawBytes);
+  };
+  auto issue_row = [&](int b, int64_t r, int p) {
+    uint64_t* bar = bars + warp * kWarpSlots + b;
+    if (cs_bulk) {
+      TCS* raw = cs_raw_of(b);
+      mbar_arrive_expect_tx(bar, row_bytes + 2 * cs_half_bytes);
+      bulk_load(raw, cosp + static_cast<int64_t>(p) * cs_ss, cs_half_bytes, bar);
+      bulk_load(raw + half, sinp + static_cast<int64_t>(p) * cs_ss, cs_half_bytes, bar);
+    } else {
+      mbar_arrive_expect_tx(bar, row_bytes);
+    }
+    bulk_load(slot_of(b), x + r * hidden, row_bytes, bar);
+  };
 
   const int64_t gw = static_cast<int64_t>(blockIdx.x) * W + warp;
   const int64_t GW = static_cast<int64_t>(gridDim.x) * W;
@@ -353,13 +383,25 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
 
   for (int i = threadIdx.x; i < hidden; i += blockDim.x) wsm[i] = load_as_float(w, i, w_dtype);
   if (lane == 0) {
-    mbar_init(full, 1);
+    for (int b = 0; b < kWarpSlots; ++b) mbar_init(bars + warp * kWarpSlots + b, 1);
     fence_mbar_init();
   }
   __syncthreads();
-  if (lane == 0 && my_rows > 0) {
-    mbar_arrive_expect_tx(full, row_bytes);
-    bulk_load(slot, x + gw * hidden, row_bytes, full);
+  int pos = static_cast<int>(gw % seq_len);
+  const int pos_step = static_cast<int>(GW % seq_len);
+  auto advance = [&](int p) {
+    p += pos_step;
+    return p >= seq_len ? p - seq_len : p;
+  };
+  // position of the row kWarpSlots rows ahead of the current one
+  int ahead_pos = pos;
+  if (lane == 0) {
+    for (int b = 0; b < kWarpSlots; ++b) {
+      if (b < my_rows) issue_row(b, gw + b * GW, ahead_pos);
+      ahead_pos = advance(ahead_pos);
+    }
+  } else {
+    for (int b = 0; b < kWarpSlots; ++b) ahead_pos = advance(ahead_pos);
   }
 
   // per-lane constants: position in head, cos / signed-sin offsets
@@ -378,19 +420,29 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
     if constexpr (MODE == 3) amax_lanes = absmax_vec<TX>(amax_lanes, make_uint4(wd[0], wd[1], wd[2], wd[3]));
   };
 
-  uint32_t par = 0;
-  int pos = static_cast<int>(gw % seq_len);
-  const int pos_step = static_cast<int>(GW % seq_len);
   int64_t row = gw;
   for (int64_t k = 0; k < my_rows; ++k, row += GW) {
-    for (int q = lane; q < 2 * half; q += 32) {
-      const int j = q < half ? q : q - half;
-      const float v = Ty<TCS>::to_f((q < half ? cosp : sinp)[static_cast<int64_t>(pos) * cs_ss + j * cs_sd]);
-      cs_buf[q] = v;
-      if (q >= half) cs_buf[q + half] = -v;
+    const int b = static_cast<int>(k % kWarpSlots);
+    const uint32_t par = static_cast<uint32_t>(k / kWarpSlots) & 1u;
+    const uint4* rv = reinterpret_cast<const uint4*>(slot_of(b));
+    if (!cs_bulk) {
+      for (int q = lane; q < 2 * half; q += 32) {
+        const int j = q < half ? q : q - half;
+        const float v = Ty<TCS>::to_f((q < half ? cosp : sinp)[static_cast<int64_t>(pos) * cs_ss + j * cs_sd]);
+        cs_buf[q] = v;
+        if (q >= half) cs_buf[q + half] = -v;
+      }
     }
-    if (!mbar_wait(full, par, err, ERR_WAIT_TIMEOUT_OTHER)) break;
-    par ^= 1u;
+
+    if (!mbar_wait(bars + warp * kWarpSlots + b, par, err, ERR_WAIT_TIMEOUT_OTHER)) break;
+    if (cs_bulk) {
+      const TCS* raw = cs_raw_of(b);
+      for (int q = lane; q < 2 * half; q += 32) {
+        const float v = Ty<TCS>::to_f(raw[q]);
+        cs_buf[q] = v;
+        if (q >= half) cs_buf[q + half] = -v;
+      }
+    }
 
     uint4 xr[VPL];
     float ss0 = 0.f, ss1 = 0.f;
@@ -405,12 +457,12 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
         ss1 = __fmaf_rn(f[e + 1], f[e + 1], ss1);
       }
     }
-    __syncwarp();  // all lanes have read the buffer: refill it with this warp's next row
-    if (lane == 0 && k + 1 < my_rows) {
+    __syncwarp();  // all lanes have read the buffers: refill them with this warp's next row
+    if (lane == 0 && k + kWarpSlots < my_rows) {
       fence_proxy_async_smem();
-      mbar_arrive_expect_tx(full, row_bytes);
-      bulk_load(slot, x + (row + GW) * hidden, row_bytes, full);
+      issue_row(b, row + kWarpSlots * GW, ahead_pos);
     }
+    ahead_pos = advance(ahead_pos);
     const float tot = warp_sum(ss0 + ss1);  // also orders this warp's cs_buf writes before the reads below
     __syncwarp();
     const float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(tot, static_cast<float>(hidden)), eps));
@@ -477,8 +529,7 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
       second_pass(std::integral_constant<bool, false>{});
     }
     __syncwarp();  // cs_buf is rewritten for the next row
-    pos += pos_step;
-    if (pos >= seq_len) pos -= seq_len;
+    pos = advance(pos);
   }
   if constexpr (MODE == 3) {
     const uint32_t b = block_max_u32(absmax_to_f32_bits<TX>(amax_lanes), qred);
@@ -565,6 +616,8 @@ cudaError_t launch_vec(const RmsNormRopeArgs& a, int threads, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
 // One CTA per SM at most, `warps` rows in flight per CTA.
 inline int64_t warp_rows_grid(int64_t rows, int warps) {
   return std::max<int64_t>(1, std::min<int64_t>((rows + warps - 1) / warps, num_sms()));
@@ -577,11 +630,15 @@ cudaError_t launch_warp_rows_m(const RmsNormRopeArgs& a, int warps, int cs_strid
   if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kern), smem); e != cudaSuccess) return e;
   const int64_t rows = a.batch * a.seq_len;
   const int64_t grid = warp_rows_grid(rows, warps);
+  // table rows by bulk copy: contiguous halves on 16-byte boundaries that fit the raw slot
+  const int64_t half_bytes = (a.head_dim / 2) * static_cast<int64_t>(sizeof(TCS));
+  const bool cs_bulk = a.cs_stride_dim == 1 && aligned16(a.cos) && aligned16(a.sin) && half_bytes % 16 == 0 &&
+                       2 * half_bytes <= kCsRawBytes && (a.cs_stride_seq * static_cast<int64_t>(sizeof(TCS))) % 16 == 0;
   kern<<<static_cast<unsigned>(grid), warps * 32, smem, st>>>(
       static_cast<const TX*>(a.x), a.weight, static_cast<const TCS*>(a.cos), static_cast<const TCS*>(a.sin),
       static_cast<TX*>(a.out), rows, static_cast<int>(a.seq_len), static_cast<int>(a.hidden),
       static_cast<int>(a.head_dim), static_cast<int>(a.num_heads * a.head_dim), a.cs_stride_seq, a.cs_stride_dim,
-      a.eps, a.w_dtype, cs_stride, error_word_ptr(), q);
+      a.eps, a.w_dtype, cs_stride, cs_bulk, error_word_ptr(), q);
   note_launch();
   return cudaGetLastError();
 }
@@ -600,12 +657,13 @@ cudaError_t launch_warp_rows_t(const RmsNormRopeArgs& a, int warps, int cs_strid
 inline int warp_rows_config(int64_t hidden, int64_t head_dim, int elem, int max_warps, int* cs_stride, size_t* smem) {
   const size_t row_bytes = static_cast<size_t>(hidden) * elem;
   *cs_stride = static_cast<int>((3 * (head_dim / 2) + 3) / 4 * 4);
-  const size_t fixed = 16 * 8 + static_cast<size_t>(hidden) * 4 + 128;
-  const size_t per_warp = row_bytes + static_cast<size_t>(*cs_stride) * 4;
+  const size_t fixed = kWarpBarBytes + static_cast<size_t>(hidden) * 4 + 128;
+  const size_t per_warp = kWarpSlots * (row_bytes + kCsRawBytes) + static_cast<size_t>(*cs_stride) * 4;
   const size_t limit = 227 * 1024 - 256;  // room for the kernel's static shared memory
   if (fixed + 8 * per_warp > limit) return 0;
   const int warps = static_cast<int>(std::min<size_t>(max_warps, (limit - fixed) / per_warp));
-  *smem = ((16 * 8 + (static_cast<size_t>(hidden) + warps * *cs_stride) * 4 + 127) / 128) * 128 + warps * row_bytes;
+  *smem = ((kWarpBarBytes + (static_cast<size_t>(hidden) + warps * *cs_stride) * 4 + 127) / 128) * 128 +
+          warps * kWarpSlots * (row_bytes + kCsRawBytes);
   return warps;
 }
 
@@ -673,8 +731,6 @@ cudaError_t launch_generic(const RmsNormRopeArgs& a, cudaStream_t st) {
   note_launch();
   return cudaGetLastError();
 }
-
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 }  // namespace
 

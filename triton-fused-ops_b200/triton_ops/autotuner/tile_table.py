@@ -12,18 +12,22 @@ from __future__ import annotations
 from typing import Dict
 
 B200_SMS = 148
+CS_RAW_BYTES = 256  # raw cos/sin slot per row buffer of the warp-per-row RMSNorm+RoPE kernel
+WARP_SLOTS = 2  # row buffers per warp of that kernel
+WARP_BAR_BYTES = 256  # its mbarrier area
 
 
 def _warp_rows_config(hidden: int, head_dim: int, elem: int, max_warps: int):
     row_bytes = hidden * elem
     cs_stride = (3 * (head_dim // 2) + 3) // 4 * 4
-    fixed = 16 * 8 + hidden * 4 + 128
-    per_warp = row_bytes + cs_stride * 4
+    fixed = WARP_BAR_BYTES + hidden * 4 + 128
+    per_warp = WARP_SLOTS * (row_bytes + CS_RAW_BYTES) + cs_stride * 4
     limit = 227 * 1024
     if fixed + 8 * per_warp > limit:
         return 0, 0
     warps = min(max_warps, (limit - fixed) // per_warp)
-    smem = ((16 * 8 + (hidden + warps * cs_stride) * 4 + 127) // 128) * 128 + warps * row_bytes
+    smem = ((WARP_BAR_BYTES + (hidden + warps * cs_stride) * 4 + 127) // 128) * 128 + warps * WARP_SLOTS * (
+        row_bytes + CS_RAW_BYTES)
     return warps, smem
 
 
