@@ -68,10 +68,13 @@ template <typename T> struct Chunk {
 // max |x| over this thread's share of x, as the fp32 bit pattern (|x| >= 0
 // orders like its bits; NaN bits exceed every finite value, as in torch's max).
 // Chunk i belongs to thread i mod stride; U chunks are loaded per iteration.
+// The vector part compares the sign-cleared bit patterns directly (per 16-bit
+// lane for 16-bit types, vmax.u16x2), which orders them like |x| without
+// converting any element; the larger lane is converted once at the end.
 template <typename T, int U>
 __device__ __forceinline__ uint32_t amax_share(const T* __restrict__ x, int64_t n, bool vec, int64_t tid,
                                                int64_t stride) {
-  uint32_t m = 0;
+  uint32_t mv = 0;  // absmax_vec lanes
   int64_t done = 0;
   if (vec) {
     const int64_t n16 = n / 16;
@@ -84,14 +87,13 @@ __device__ __forceinline__ uint32_t amax_share(const T* __restrict__ x, int64_t 
       }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        float f[16];
-        c[u].to_f(f);
 #pragma unroll
-        for (int j = 0; j < 16; ++j) m = max(m, __float_as_uint(fabsf(f[j])));
+        for (int q = 0; q < Chunk<T>::VECS; ++q) mv = absmax_vec<T>(mv, c[u].v[q]);
       }
     }
     done = n16 * 16;
   }
+  uint32_t m = absmax_to_f32_bits<T>(mv);
   for (int64_t i = done + tid; i < n; i += stride) m = max(m, __float_as_uint(fabsf(Ty<T>::to_f(x[i]))));
   return m;
 }
@@ -301,81 +303,6 @@ template <typename T>
 __device__ __forceinline__ void store_codes16(uint8_t* out, int64_t v, const uint32_t (&w)[2]) {
   if constexpr (sizeof(T) == 2) reinterpret_cast<uint2*>(out)[v] = make_uint2(w[0], w[1]);
   else reinterpret_cast<uint32_t*>(out)[v] = w[0];
-}
-
-// ---- dynamic-scale quantize with the tensor resident in shared memory -----
-// For tensors that fit in the SMs' shared memory (one CTA per SM, up to
-// kResSlabMax bytes each): every CTA bulk-copies its contiguous slab into
-// shared memory in kResPieces pieces (one mbarrier each) and folds each piece
-// into its max |x| as it lands; CTAs meet at the grid barrier; then each CTA
-// encodes its slab from shared memory. HBM sees one read of x and one write
-// of the codes. 16-byte vectors; the last CTA also covers the n % 16 tail
-// elements from global memory.
-constexpr int kResThreads = 1024;
-constexpr int kResPieces = 16;
-constexpr size_t kResSlabMax = 227 * 1024 - 1024;
-
-template <typename T, bool E4M3>
-__global__ void __launch_bounds__(kResThreads, 1)
-    quantize_resident_kernel(const T* __restrict__ x, int64_t n, int64_t vecs_per_cta, uint32_t* __restrict__ barrier,
-                             float* __restrict__ scale_out,
-                             uint8_t* __restrict__ out, uint32_t* __restrict__ err) {
-  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
-  constexpr int EV = 16 / sizeof(T);  // elements per 16-byte vector
-  extern __shared__ __align__(128) uint4 slab[];
-  __shared__ uint64_t bars[kResPieces];
-  __shared__ uint32_t red[32];
-  __shared__ float s_sh;
-  __shared__ int ok_sh;
-  const int64_t nvec = n / EV;
-  const int64_t v0 = static_cast<int64_t>(blockIdx.x) * vecs_per_cta;
-  const int64_t v1 = min(nvec, v0 + vecs_per_cta);
-  const int my = v1 > v0 ? static_cast<int>(v1 - v0) : 0;
-  const int per_piece = (my + kResPieces - 1) / kResPieces;
-  if (threadIdx.x == 0) {
-    for (int p = 0; p < kResPieces; ++p) mbar_init(&bars[p], 1);
-    fence_mbar_init();
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int p = 0; p < kResPieces; ++p) {
-      const int a = p * per_piece, b = min(my, a + per_piece);
-      const uint32_t bytes = static_cast<uint32_t>(max(0, b - a)) * 16u;
-      if (bytes > 0) {
-        mbar_arrive_expect_tx(&bars[p], bytes);
-        bulk_load(slab + a, reinterpret_cast<const uint4*>(x) + v0 + a, bytes, &bars[p]);
-      } else {
-        mbar_arrive(&bars[p]);
-      }
-    }
-  }
-  uint32_t m = 0;
-  for (int p = 0; p < kResPieces; ++p) {
-    mbar_wait(&bars[p], 0, err, ERR_WAIT_TIMEOUT_OTHER);  // on expiry: error bit set, values unreliable
-    const int a = p * per_piece, b = min(my, a + per_piece);
-    for (int v = a + threadIdx.x; v < b; v += kResThreads) m = absmax_vec<T>(m, slab[v]);
-  }
-  uint32_t mf = absmax_to_f32_bits<T>(m);
-  if (blockIdx.x == gridDim.x - 1)
-    for (int64_t i = nvec * EV + threadIdx.x; i < n; i += kResThreads)
-      mf = max(mf, __float_as_uint(fabsf(Ty<T>::to_f(x[i]))));
-  const uint32_t bmax = block_max_u32(mf, red);
-  if (!grid_max_scale(bmax, barrier, err, &s_sh, &ok_sh)) return;
-  const float s = s_sh;
-  if (threadIdx.x == 0 && blockIdx.x == 0) *scale_out = s;
-  const bool in_range = (s > 0.f && s < INFINITY);
-  for (int v = threadIdx.x; v < my; v += kResThreads) {
-    uint32_t w[2];
-    encode_vec16<T, E4M3>(slab[v], s, in_range, w);
-    store_codes16<T>(out, v0 + v, w);
-  }
-  if (blockIdx.x == gridDim.x - 1) {
-    for (int64_t i = nvec * EV + threadIdx.x; i < n; i += kResThreads) {
-      const float c = __fmul_rn(Ty<T>::to_f(x[i]), s);
-      out[i] = static_cast<uint8_t>(E4M3 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(c, __NV_SATFINITE, __NV_E4M3))
-                                         : ref_encode(c));
-    }
-  }
 }
 
 // ---- dynamic-scale quantize of small tensors: one cluster, no grid barrier --
@@ -819,46 +746,6 @@ cudaError_t quant_dyn_t(const void* x, int64_t n, float* scale_out, void* out, v
   note_launch();
   return e;
 }
-// The shared-memory-resident variant, when x (16-byte aligned) fits in the
-// SMs' shared memory and is at least 64 vectors per SM; *used tells whether
-// it was launched.
-template <typename T, bool E4M3>
-cudaError_t quant_res_t(const void* x, int64_t n, float* scale_out, void* out, void* ws, size_t ws_bytes,
-                        cudaStream_t st, bool* used) {
-  *used = false;
-  constexpr int EV = 16 / sizeof(T);
-  const int sms = num_sms();
-  const int64_t nvec = n / EV;
-  if (!al16(x) || !al16(out) || nvec < 64ll * sms) return cudaSuccess;
-  const int64_t vpc = (nvec + sms - 1) / sms;
-  const size_t smem = static_cast<size_t>(vpc) * 16;
-  if (smem > kResSlabMax) return cudaSuccess;
-  const int grid = static_cast<int>((nvec + vpc - 1) / vpc);
-  if (ws_bytes < kQuantPartialsOffset + sizeof(uint32_t) * static_cast<size_t>(grid)) return cudaErrorInvalidValue;
-  auto kernel = quantize_resident_kernel<T, E4M3>;
-  if (cudaError_t e = ensure_smem_attr(reinterpret_cast<const void*>(kernel), kResSlabMax); e != cudaSuccess)
-    return e;
-  auto* barrier = static_cast<uint32_t*>(ws);
-  cudaError_t e = cudaMemsetAsync(barrier, 0, 2 * sizeof(uint32_t), st);  // counter + max
-  note_launch();
-  if (e != cudaSuccess) return e;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(kResThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kernel, static_cast<const T*>(x), n, vpc, barrier, scale_out,
-                         static_cast<uint8_t*>(out), error_word_ptr());
-  note_launch();
-  *used = true;
-  return e;
-}
-
 // The one-cluster form for small aligned tensors of whole vectors; *used
 // tells whether it was launched.
 template <typename T, bool E4M3>
@@ -895,11 +782,13 @@ cudaError_t quant_small_t(const void* x, int64_t n, float* scale_out, void* out,
 
 // Mid-size tensors (above the one-cluster form, up to kMidMaxBytes): two
 // ordinary launches, per-CTA amax partials then an encode that reduces them
-// (re-reading x, from L2 at these sizes). No barrier memset, no cooperative
-// launch: at [1024, 4096] fp16 8.3 us against 14.2 us for the resident form,
-// which only pays off once x is large enough for its single HBM read to
-// matter.
-constexpr int64_t kMidMaxBytes = 16ll << 20;
+// (re-reading x, which at these sizes is still in L2). No barrier memset, no
+// cooperative launch. [4096, 4096] fp16 (32 MiB): 16.7 us (e4m3 14.5 us)
+// against 18.7 / 17.4 us for a cooperative one-kernel form that kept x in
+// shared memory over a grid barrier (one HBM read, but the slab load, the
+// barrier and the encode ran back to back). Larger tensors no longer fit L2
+// reliably and take the grid-barrier form below.
+constexpr int64_t kMidMaxBytes = 48ll << 20;
 
 template <typename T, bool E4M3>
 cudaError_t quant_any_t(const void* x, int64_t n, float* scale_out, void* out, void* ws, size_t ws_bytes,
@@ -917,8 +806,6 @@ cudaError_t quant_any_t(const void* x, int64_t n, float* scale_out, void* out, v
     return encode_launch(x, n, x_dtype, nullptr, parts, nparts, scale_out, out,
                          E4M3 ? static_cast<int>(DType::E4M3) : static_cast<int>(DType::U8), st);
   }
-  e = quant_res_t<T, E4M3>(x, n, scale_out, out, ws, ws_bytes, st, &used);
-  if (e != cudaSuccess || used) return e;
   return quant_dyn_t<T, E4M3>(x, n, scale_out, out, ws, ws_bytes, st);
 }
 }  // namespace
