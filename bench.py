@@ -420,6 +420,24 @@ def time_graph(calls, reps: int = 20):
     return us, None
 
 
+def host_us_per_call(fn, calls: int = 200) -> float:
+    """Host (CPU) microseconds per call: wall clock over back-to-back calls that
+    are not synchronised, so the GPU runs behind and the Python, validation,
+    allocation and launch work of each call is what is timed (one warm-up
+    round first; the launch queue holds them all)."""
+    import torch
+
+    for _ in range(20):
+        fn()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    for _ in range(calls):
+        fn()
+    t1 = time.perf_counter()
+    torch.cuda.synchronize()
+    return (t1 - t0) * 1e6 / calls
+
+
 def _copies(make, nbytes_each: int, min_total: int = 2 * L2_BYTES, cap: int = 128):
     """Enough independent tensors from make() that together they exceed min_total bytes."""
     n = max(2, min(cap, -(-min_total // max(1, nbytes_each))))
@@ -431,9 +449,11 @@ def components(peaks, flush_buf):
 
     For each op: ``us`` = device time per call from CUDA-graph replay over
     rotating inputs larger than L2 (the kernel-side number the roofline
-    fraction uses), ``us_call`` = one call through the Python API timed alone
-    with CUDA events after an L2 flush (includes host overhead and launch
-    latency).
+    fraction uses), ``us_call`` = one eager call through the Python API timed
+    alone with CUDA events after an L2 flush (device-side: the flush kernel is
+    still running when the call's launches are queued, so this adds cold-L2
+    inputs and the gaps between eager launches, not host time), and for the
+    decode-size calls ``host_us`` = host time per call (see host_us_per_call).
     """
     import torch
 
@@ -495,10 +515,13 @@ def components(peaks, flush_buf):
     us, err = time_graph([lambda x=x: triton_ops.quantize_fp8(x) for x in xd])
     us_call = 1e3 * time_events(lambda: triton_ops.quantize_fp8(xd[0]), 30, flush_buf)
     out["fp8_quantize_16x4096"] = entry(us, err, us_call, nbytes=3 * 16 * 4096)
+    out["fp8_quantize_16x4096"]["host_us"] = host_us_per_call(lambda: triton_ops.quantize_fp8(xd[0]))
     lin = triton_ops.FP8Linear(4096, 4096, bias=True).to(dev).half()
     us, err = time_graph([lambda x=x: lin(x) for x in xd])
     us_call = 1e3 * time_events(lambda: lin(xd[0]), 30, flush_buf)
     out["fp8linear_16x4096x4096"] = entry(us, err, us_call, flops=2.0 * 16 * 4096 * 4096)
+    out["fp8linear_16x4096x4096"]["host_us"] = host_us_per_call(lambda: lin(xd[0]))
+    out["native_extension_loaded"] = _lib_ext_loaded()
     del xd, lin
 
     # per-token scales at [4096, 4096] fp16: the row scales, then quantize and
@@ -660,6 +683,12 @@ def add_cpu_numbers(comps, cpu, threads):
             e["cpu_kind"] = kind + (" (fp32 input)" if name == "rmsnorm_rope_2x128x4096" else "")
             if e.get("us"):
                 e["gpu_speedup_vs_cpu"] = cpu_us / e["us"]
+
+
+def _lib_ext_loaded() -> bool:
+    from triton_ops import _lib
+
+    return _lib.ext() is not None
 
 
 def read_traffic():

@@ -74,3 +74,32 @@ def test_workspace_queries():
     assert lib.tfo_fp8_gemm_workspace_bytes(128, 256, 100, 3, 0) >= 128 * 112 + 256 * 112
     assert lib.tfo_gated_mlp_workspace_bytes(64, 64, 64, 0, 0) == 0  # fp16 x fp16: no copies
     assert lib.tfo_gated_mlp_workspace_bytes(64, 64, 64, 0, 2) >= 64 * 64 * 4  # fp16 x with fp32 weights
+
+
+def test_extension_loads_and_declines_what_it_does_not_serve():
+    """The PyTorch extension is built in-tree, links the same library, and returns None
+    (so that the Python wrapper validates and raises) for inputs outside its common case."""
+    import torch
+
+    from triton_ops import _lib
+
+    ext = _lib.ext()
+    assert ext is not None, "build the extension with triton-fused-ops_b200/build.py"
+    for name in ("quantize_dynamic", "linear_prepared", "clear_workspaces"):
+        assert hasattr(ext, name)
+    assert ext.quantize_dynamic(torch.zeros(4), _lib.U8) is None  # CPU tensor
+    w = torch.zeros(8, 16, dtype=torch.int8)
+    assert ext.linear_prepared(torch.zeros(2, 16), w, torch.zeros(8, dtype=torch.int32), torch.ones(()), None) is None
+    _lib.clear_workspaces()
+
+
+def test_extension_errors_map_to_package_exceptions():
+    import pytest
+
+    from triton_ops import _lib
+    from triton_ops.exceptions import TritonKernelError, UnsupportedDtypeError
+
+    with pytest.raises(UnsupportedDtypeError):
+        _lib.raise_ext_error(RuntimeError("tfo status 2: tfo_fp8_quantize: x must be f16, bf16 or f32"))
+    with pytest.raises(TritonKernelError, match="status 3"):
+        _lib.raise_ext_error(RuntimeError("tfo status 3: tfo_fp8_quantize: out of memory"))

@@ -1,9 +1,11 @@
-"""Builds the sm_100a shared library ``triton_ops/_lib/libtfo_b200.so``.
+"""Builds the sm_100a shared library ``triton_ops/_lib/libtfo_b200.so`` and its PyTorch extension.
 
 Every ``csrc/*.cu`` file is compiled by nvcc for ``sm_100a`` only (no PTX
 fallback, no other architecture) and linked into one shared library that
-exports the C ABI declared in ``include/tfo_b200.h``. Objects are rebuilt only
-when a source or header is newer than the library.
+exports the C ABI declared in ``include/tfo_b200.h``. ``csrc_ext/tfo_ext.cpp``
+is then compiled against torch's headers into ``triton_ops/_lib/_tfo_ext*.so``
+(linked to the library), the fast entry points for launch-latency-bound calls.
+Each is rebuilt only when a source or header is newer than it.
 
 Usage: ``python build.py [--force] [--jobs N]``
 """
@@ -70,8 +72,55 @@ def _compile(nvcc: str, src: Path, log_dir: Path) -> Path:
     return obj
 
 
+EXT_SRC = HERE / "csrc_ext" / "tfo_ext.cpp"
+
+
+def _ext_path() -> Path:
+    import sysconfig
+
+    return LIB_DIR / ("_tfo_ext" + sysconfig.get_config_var("EXT_SUFFIX"))
+
+
+def build_ext(force: bool = False) -> Path:
+    """Compiles the PyTorch extension (``_tfo_ext``) over the C ABI, linked to the library."""
+    import sysconfig
+
+    import torch
+    from torch.utils import cpp_extension as ce
+
+    out = _ext_path()
+    deps = [EXT_SRC, LIB_PATH, INCLUDE / "tfo_b200.h", Path(__file__)]
+    if not force and out.exists() and all(p.stat().st_mtime <= out.stat().st_mtime for p in deps):
+        return out
+    try:
+        inc = ce.include_paths(device_type="cuda")
+    except TypeError:  # older torch
+        inc = ce.include_paths(cuda=True)
+    torch_lib = ce.library_paths()[0]
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-fvisibility=hidden",
+           f"-D_GLIBCXX_USE_CXX11_ABI={int(torch._C._GLIBCXX_USE_CXX11_ABI)}",
+           "-DTORCH_EXTENSION_NAME=_tfo_ext", "-DTORCH_API_INCLUDE_EXTENSION_H"]
+    for i in [*inc, sysconfig.get_paths()["include"], str(INCLUDE)]:
+        cmd += ["-I", i]
+    tmp = out.with_suffix(".tmp")
+    cmd += [str(EXT_SRC), "-o", str(tmp), "-L", torch_lib, "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+            "-ltorch_cuda", "-ltorch_python", "-L", str(LIB_DIR), "-ltfo_b200", "-Wl,-rpath,$ORIGIN",
+            f"-Wl,-rpath,{torch_lib}"]
+    res = subprocess.run(cmd, capture_output=True, text=True)
+    if res.returncode != 0:
+        raise RuntimeError(f"extension build failed:\n{res.stderr[-6000:]}")
+    os.replace(tmp, out)
+    return out
+
+
 def build(force: bool = False, jobs: int | None = None, verbose: bool = False) -> Path:
-    """Compiles and links the library if it is out of date; returns its path."""
+    """Compiles and links the library (and then the extension) if out of date; returns the library's path."""
+    _build_lib(force, jobs, verbose)
+    build_ext(force)
+    return LIB_PATH
+
+
+def _build_lib(force: bool, jobs: int | None, verbose: bool) -> Path:
     if not _needs_build(force):
         return LIB_PATH
     nvcc = _nvcc()

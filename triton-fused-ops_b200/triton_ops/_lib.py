@@ -139,6 +139,53 @@ def load() -> ctypes.CDLL:
         return lib
 
 
+_ext = None
+_ext_tried = False
+
+
+def ext():
+    """The PyTorch extension over the C ABI (``_lib/_tfo_ext*.so``), or None.
+
+    It serves the launch-latency-bound calls (dynamic quantize, FP8Linear's
+    forward) in one C++ call; without it those calls take the ctypes path,
+    which runs the same kernels. Not used when ``TFO_B200_LIB`` points the
+    ctypes binding at another library, so that both always use one library.
+    """
+    global _ext, _ext_tried
+    if _ext_tried:
+        return _ext
+    load()  # the extension links this library: load it first (outside _lock, which load() takes)
+    with _lock:
+        if _ext_tried:
+            return _ext
+        override = os.environ.get("TFO_B200_LIB")
+        paths = sorted(LIB_PATH.parent.glob("_tfo_ext*.so"))
+        if paths and (override is None or Path(override).resolve() == LIB_PATH.resolve()):
+            import importlib.util
+
+            spec = importlib.util.spec_from_file_location("triton_ops._tfo_ext", paths[0])
+            mod = importlib.util.module_from_spec(spec)
+            try:
+                spec.loader.exec_module(mod)
+                _ext = mod
+            except ImportError:  # pragma: no cover - a stale build for another torch
+                _ext = None
+        _ext_tried = True
+        return _ext
+
+
+def raise_ext_error(exc: RuntimeError):
+    """Re-raises an extension error ("tfo status <n>: ...") as the package's exception for that status."""
+    msg = str(exc)
+    if msg.startswith("tfo status "):
+        status = int(msg.split()[2].rstrip(":"))
+        text = msg.split(": ", 1)[1] if ": " in msg else msg
+        if status == ERR_DTYPE:
+            raise UnsupportedDtypeError(text) from exc
+        raise TritonKernelError(f"{text} (status {status})") from exc
+    raise exc
+
+
 def declared_symbols() -> list[str]:
     return list(_SIGNATURES)
 
@@ -249,3 +296,5 @@ def clear_workspaces() -> None:
     """Releases every cached scratch buffer (they return to torch's caching allocator)."""
     with _ws_lock:
         _ws_cache.clear()
+    if _ext is not None:
+        _ext.clear_workspaces()

@@ -229,6 +229,19 @@ class FP8Linear(torch.nn.Module):
         return self._prepared[1], self._prepared[2]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        prep = self._prepared
+        if prep is not None:
+            w = self.weight_fp8
+            fast = _lib.ext()
+            if fast is not None and prep[0] == (w.data_ptr(), w._version, w.device):
+                # the weight is unchanged since it was prepared: quantize x, GEMM and
+                # bias in one C++ call (None outside the common case)
+                try:
+                    out = fast.linear_prepared(x, prep[1], prep[2], self.weight_scale, self.bias)
+                except RuntimeError as exc:
+                    _lib.raise_ext_error(exc)
+                if out is not None:
+                    return out
         self.quantize_weights()
         orig_shape = x.shape
         x_2d = x.reshape(-1, self.in_features)

@@ -37,6 +37,7 @@ dequantize_fp8_kernel = NativeKernel("dequantize_fp8_kernel", "tfo_fp8_dequantiz
 compute_scale_kernel = NativeKernel("compute_scale_kernel", "tfo_fp8_compute_scale", "grid-wide amax -> scale")
 
 _CODE_DTYPES = (torch.uint8,) + ((torch.float8_e4m3fn,) if hasattr(torch, "float8_e4m3fn") else ())
+_QCODE = {torch.uint8: _lib.U8, **({torch.float8_e4m3fn: _lib.E4M3} if hasattr(torch, "float8_e4m3fn") else {})}
 
 
 def _row_scales(tensor: torch.Tensor, scale: torch.Tensor):
@@ -77,6 +78,16 @@ def quantize_fp8(
         (codes shaped like `tensor`, scale) — the scale is the tensor passed in,
         or a new 0-dim fp32 CUDA tensor.
     """
+    if scale is None:
+        fast = _lib.ext()
+        if fast is not None:
+            # one C++ call for the common case (CUDA, contiguous, float input, known code dtype)
+            try:
+                r = fast.quantize_dynamic(tensor, _QCODE.get(dtype, -1))
+            except RuntimeError as exc:
+                _lib.raise_ext_error(exc)
+            if r is not None:
+                return r
     validate_fp8_quantize_inputs(tensor, scale)
     if dtype not in _CODE_DTYPES:
         raise UnsupportedDtypeError(
