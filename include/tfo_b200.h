@@ -65,7 +65,7 @@ TFO_API int tfo_device_error_flags(uint32_t* flags, int clear);
 
 /* The launch configuration the library picks for a problem shape: the static,
  * shape-keyed table that replaces the reference's autotuner
- * (triton_ops/autotuner/autotuner.py; its ops launch fixed block sizes).
+ * (triton_ops/autotuner/tuner.py; its ops launch fixed block sizes).
  *   op TFO_OP_FP8_GEMM:     M, N, K, aux = TFO_DTYPE_U8 or _E4M3 ([K, N] B,
  *                           16-byte-aligned operands);
  *                           out = {tile rows, tile columns, CTAs per MMA,
@@ -148,7 +148,7 @@ TFO_API int tfo_fp8_quantize(const void* x, int64_t numel, int x_dtype, const fl
  * amax partials) is a static 16 KiB device array inside this library, which
  * every GPU that loads the library keeps until the process exits. Limit: a
  * call may need at most 4096 partial slots (one per amax block, at most
- * 2 x the SM count, i.e. 296 on a 148-SM B200); larger needs are rejected with
+ * 4 x the SM count, i.e. 592 on a 148-SM B200); larger needs are rejected with
  * TFO_ERR_INVALID and an explanatory message. The first call in each CUDA
  * context (per device, and again after cudaDeviceReset or in another context
  * made current through the driver API) looks up the scratch address in that
