@@ -334,3 +334,46 @@ def test_fp8linear_prepared_and_unaligned_in_features(cuda):
     y1 = lin2(x2)
     lin2.weight_fp8.fill_(128)  # in place (code 128 decodes to 0): the next forward must see it
     assert torch.equal(lin2(x2), torch.zeros_like(y1))
+
+
+# Few-row products with a K-major [N, K] B (FP8Linear's layout) against the
+# oracle: codec (exact int32 sums) and e4m3, ragged N and M = 1.
+@pytest.mark.parametrize("M,N,K", [(16, 4096, 4096), (1, 4096, 1024), (32, 2390, 4096), (7, 3000, 272)])
+@pytest.mark.parametrize("qdt", [torch.uint8, torch.float8_e4m3fn])
+def test_few_rows_nk_b_match_oracle(cuda, M, N, K, qdt):
+    from triton_ops import _lib, quantize_fp8
+    from triton_ops.kernels.fp8_gemm import _gemm_codes
+
+    g = torch.Generator(device="cuda").manual_seed(M * 7 + N)
+    qa, sa = quantize_fp8(torch.randn(M, K, device="cuda", generator=g).half(), dtype=qdt)
+    qb, sb = quantize_fp8(torch.randn(N, K, device="cuda", generator=g).half(), dtype=qdt)  # [N, K]
+    out = host(_gemm_codes(qa, qb, sa, sb, torch.float32, _lib.B_NK))
+    a_u8, b_u8 = qa.view(torch.uint8).cpu().numpy(), qb.view(torch.uint8).cpu().numpy()
+    if qdt == torch.uint8:
+        ref = O.fp8_gemm(a_u8, b_u8.T, sa.item(), sb.item(), "f32")
+    else:
+        ref = O.fp8_gemm_e4m3(a_u8, b_u8.T, sa.item(), sb.item(), "f32")
+    assert O.rel_fro(out, ref) <= 1e-5
+    out16 = host(_gemm_codes(qa, qb, sa, sb, torch.float16, _lib.B_NK))
+    assert O.rel_fro(out16, ref) <= 1e-3
+    assert _lib.device_error_flags() == 0
+
+
+@pytest.mark.parametrize("M", [1, 16, 32])
+def test_prepared_linear_with_bias_matches_oracle(cuda, M):
+    """FP8Linear(4096, 4096, bias) at decode sizes (prepared int8 weight, raw u8 activations,
+    per-column correction, bias in the epilogue) against the oracle's GEMM plus the bias."""
+    from triton_ops import FP8Linear, quantize_fp8
+
+    torch.manual_seed(M)
+    lin = FP8Linear(4096, 4096, bias=True).cuda()
+    with torch.no_grad():
+        lin.bias.normal_()
+    x = torch.randn(M, 4096, device="cuda", dtype=torch.float16)
+    y = lin(x)
+    y = lin(x)  # second call: the prepared weight (the first call quantizes and prepares it)
+    qx, sx = quantize_fp8(x)
+    ref = O.fp8_gemm(qx.cpu().numpy(), lin.weight_fp8.cpu().numpy().T, sx.item(), lin.weight_scale.item(), "f16")
+    ref = O.round_to(ref + host(lin.bias), "f32")  # fp16 product + fp32 bias -> fp32 (torch's promotion)
+    assert y.dtype == torch.float32 and y.shape == (M, 4096)
+    assert O.rel_fro(host(y), ref) <= 1e-3
