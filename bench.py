@@ -577,7 +577,31 @@ def components(peaks, flush_buf):
         except Exception as exc:  # noqa: BLE001 - comparator only
             lib8[str(M)] = {"error": f"{type(exc).__name__}: {exc}"[:200]}
         del qa, qa8, a_f
-    del bs, bs8, bs8_nk
+    # the same products with B given as [N, K] (K-major: FP8Linear's weight
+    # layout, and the layout of the cuBLASLt comparator above), small M
+    from triton_ops.kernels.fp8_gemm import _gemm_codes
+    from triton_ops import _lib as tfo_lib
+    bs_nk = [(q.t().contiguous(), s_) for q, s_ in bs]
+    gemm_nk, gemm8_nk = {}, {}
+    for M in (16, 32, 128, 1024):
+        fl = 2.0 * M * 4096 * 4096
+        a_f = _copies(lambda: torch.randn(M, 4096, device=dev, generator=g).half(), M * 4096, cap=len(bs))
+        a_f = (a_f * ((len(bs) + len(a_f) - 1) // len(a_f)))[: len(bs)]
+        for table, qd, bl in ((gemm_nk, torch.uint8, bs_nk), (gemm8_nk, torch.float8_e4m3fn, bs8_nk)):
+            qa = [triton_ops.quantize_fp8(a, dtype=qd) for a in a_f]
+            us, err = time_graph([lambda a=a, b=b: _gemm_codes(a[0], b[0], a[1], b[1], torch.float16, tfo_lib.B_NK)
+                                  for a, b in zip(qa, bl)])
+            e = entry(us, err, None, flops=fl)
+            if us is not None and M <= 128:
+                nbytes = M * 4096 + 4096 * 4096 + 2 * M * 4096
+                ach = nbytes / us / 1e3
+                e["roofline"] = {"bound": "hbm", "achieved": ach, "peak": hbm, "unit": "GB/s", "frac": ach / hbm,
+                                 "algorithmic_bytes": nbytes, "peak_source": f"{peaks['source']} hbm_gbs"}
+            table[str(M)] = e
+        del a_f
+    out["fp8_gemm_nk_Mx4096x4096"] = gemm_nk
+    out["fp8_gemm_nk_e4m3_Mx4096x4096"] = gemm8_nk
+    del bs, bs8, bs8_nk, bs_nk
     # FP8 tensor peak measured in this run: the library fp8 GEMM (cuBLASLt
     # through torch._scaled_mm, e4m3, fp32 accumulate) at 8192^3, best of 10
     # back-to-back launches (a burst, like the bf16 peak); 2 x the measured

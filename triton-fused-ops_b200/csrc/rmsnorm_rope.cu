@@ -395,13 +395,9 @@ __global__ void __launch_bounds__(32 * warp_rows_max_warps(VPL), 1) rmsnorm_rope
   };
   // position of the row kWarpSlots rows ahead of the current one
   int ahead_pos = pos;
-  if (lane == 0) {
-    for (int b = 0; b < kWarpSlots; ++b) {
-      if (b < my_rows) issue_row(b, gw + b * GW, ahead_pos);
-      ahead_pos = advance(ahead_pos);
-    }
-  } else {
-    for (int b = 0; b < kWarpSlots; ++b) ahead_pos = advance(ahead_pos);
+  for (int b = 0; b < kWarpSlots; ++b) {
+    if (lane == 0 && b < my_rows) issue_row(b, gw + b * GW, ahead_pos);
+    ahead_pos = advance(ahead_pos);
   }
 
   // per-lane constants: position in head, cos / signed-sin offsets
