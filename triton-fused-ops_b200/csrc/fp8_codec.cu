@@ -599,6 +599,15 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __re
   // data-dependent lookups of a warp never collide on a shared-memory bank.
   __shared__ R base[256];
   __shared__ uint32_t lut[256 * 32];
+  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+  const int64_t n16 = vec ? n / 16 : 0;
+  // this thread's first U code vectors are requested before the table is
+  // built, so the table's construction overlaps their DRAM latency
+  uint4 in[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u)
+    if (tid + u * stride < n16) in[u] = __ldcs(reinterpret_cast<const uint4*>(q) + tid + u * stride);
   const float s = *scale;
   for (int u = threadIdx.x; u < 256; u += blockDim.x) {
     float v;
@@ -614,17 +623,15 @@ __global__ void __launch_bounds__(kDecThreads) decode_kernel(const uint8_t* __re
   for (int i = threadIdx.x; i < 256 * 32; i += blockDim.x) lut[i] = base[i >> 5];
   __syncthreads();
   const uint32_t* my_lut = lut + (threadIdx.x & 31);
-  const int64_t tid = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
   constexpr int OV = 16 * sizeof(R) / 16;  // 16-byte output vectors per code vector
   int64_t done = 0;
   if (vec) {
-    const int64_t n16 = n / 16;
     for (int64_t i = tid; i < n16; i += U * stride) {
-      uint4 in[U];
+      if (i != tid) {
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (i + u * stride < n16) in[u] = __ldcs(reinterpret_cast<const uint4*>(q) + i + u * stride);
+        for (int u = 0; u < U; ++u)
+          if (i + u * stride < n16) in[u] = __ldcs(reinterpret_cast<const uint4*>(q) + i + u * stride);
+      }
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         if (i + u * stride < n16) {
