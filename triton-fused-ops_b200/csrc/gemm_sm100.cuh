@@ -52,11 +52,14 @@ struct TileSched {
 
 // Per-CTA shared-memory layout. The UMMA is M = 128 * CG by N = NUM_B *
 // BLOCK_N; each CTA stages A_ROWS rows of A and N / CG rows of B per K block.
-// A_ROWS < 128 (one CTA per MMA, M <= A_ROWS): the A stages are packed
-// closer, so more stages fit; the MMA still reads 128 rows from a stage's
-// start, the rows past A_ROWS being whatever follows in shared memory (later
-// A stages, then the first B stage: always inside the allocation), and the
-// accumulator rows they feed lie past M and are never stored.
+// Stage s is [A_ROWS rows of A | B tile] at s * STAGE_BYTES.
+// A_ROWS < 128 (one CTA per MMA, M <= A_ROWS): the A stages are smaller, so
+// more stages fit; the MMA still reads 128 rows from the A tile's start, and
+// the rows past A_ROWS are the first bytes of the same stage's B tile. Those
+// landed before the MMA's wait on the stage's full barrier and are not
+// rewritten before the MMA commits the stage as empty, so the extra rows read
+// settled memory; the accumulator rows they feed lie past M and are never
+// stored or exchanged.
 template <int BLOCK_N, int NUM_B, int STAGES, int CG = 1, bool KSPLIT = false, int A_ROWS = 128>
 struct GemmLayout {
   static constexpr int BM = 128;             // accumulator lanes (output rows) per CTA
@@ -85,8 +88,9 @@ struct GemmLayout {
   static constexpr int SUM_OFFSET = RED_BYTES;
   static constexpr int SUM_BYTES = KSPLIT ? (BM / 2) * N_MMA * 4 : 0;
   static_assert(RED_BYTES + SUM_BYTES <= RING_BYTES, "reduction tiles fit in the ring");
-  static_assert(STAGES * A_BYTES + STAGES * B_STAGE_BYTES >= (STAGES - 1) * A_BYTES + BM * 128,
-                "a 128-row read from the last A stage stays inside the ring");
+  static_assert(A_ROWS == BM || STAGE_BYTES >= BM * 128,
+                "a 128-row read from a short A tile stays inside its own stage");
+  static_assert(A_BYTES % 1024 == 0 && B_STAGE_BYTES % 1024 == 0, "128-byte-swizzled tiles on 1 KB boundaries");
   static constexpr int BAR_OFFSET = RING_BYTES;
   // dynamic shared memory: ring + barriers + 1 KB for manual alignment
   static constexpr size_t SMEM_BYTES = static_cast<size_t>(BAR_OFFSET) + 256 + 1024;
@@ -185,8 +189,9 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // stage s: A tile at sa + s * STAGE_BYTES, B tile at sb + s * STAGE_BYTES
   uint8_t* sa = smem;
-  uint8_t* sb = smem + STAGES * L::A_BYTES;
+  uint8_t* sb = smem + L::A_BYTES;
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::BAR_OFFSET);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
@@ -274,8 +279,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
           const uint32_t ph = (it / STAGES) & 1;
           if (!wait_or_abort(&empty[s], ph ^ 1, abort_flag, err, ERR_WAIT_TIMEOUT_PRODUCER)) break;
           const int kx = kb * KB_ELEMS;
-          uint8_t* a_dst = sa + s * L::A_BYTES;
-          uint8_t* b_dst = sb + s * L::B_STAGE_BYTES;
+          uint8_t* a_dst = sa + s * L::STAGE_BYTES;
+          uint8_t* b_dst = sb + s * L::STAGE_BYTES;
           if constexpr (CG == 1) {
             mbar_arrive_expect_tx(&full[s], L::STAGE_BYTES);
             tma_load_2d(a_dst, &tmap_a, &full[s], kx, m_row);
@@ -326,8 +331,8 @@ __global__ void __launch_bounds__(gemm_threads(EPI_WARPS), 1)
           const uint32_t ph = (it / STAGES) & 1;
           if (!wait_or_abort(&full[s], ph, abort_flag, err, ERR_WAIT_TIMEOUT_MMA)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t a_addr = smem_u32(sa + s * L::A_BYTES);
-          const uint32_t b_addr = smem_u32(sb + s * L::B_STAGE_BYTES);
+          const uint32_t a_addr = smem_u32(sa + s * L::STAGE_BYTES);
+          const uint32_t b_addr = smem_u32(sb + s * L::STAGE_BYTES);
           // With CG == 1 the NUM_B B tiles of a stage are consecutive
           // 128-byte-swizzled K-major tiles, i.e. one (NUM_B * BLOCK_N)-row
           // tile, so a single UMMA of N = NUM_B * BLOCK_N reads the A tile
