@@ -535,6 +535,12 @@ def components(peaks, flush_buf):
     us, err = time_graph([lambda x=x, s=s: triton_ops.quantize_fp8(x, s) for x, s in zip(xr, rs)])
     us_call = 1e3 * time_events(lambda: triton_ops.quantize_fp8(xr[0], rs[0]), 30, flush_buf)
     out["fp8_quantize_rows_4096x4096"] = entry(us, err, us_call, nbytes=3 * 4096 * 4096)
+    # per-token dynamic quantize in one launch, against the two calls it replaces
+    us, err = time_graph([lambda x=x: triton_ops.quantize_fp8_per_token(x) for x in xr])
+    us_call = 1e3 * time_events(lambda: triton_ops.quantize_fp8_per_token(xr[0]), 30, flush_buf)
+    e = entry(us, err, us_call, nbytes=3 * 4096 * 4096)
+    e["two_calls_us"], _ = time_graph([lambda x=x: triton_ops.quantize_fp8(x, per_row(x, dim=-1)) for x in xr])
+    out["fp8_quantize_per_token_4096x4096"] = e
     qr = [triton_ops.quantize_fp8(x, s)[0] for x, s in zip(xr, rs)]
     del xr
     us, err = time_graph([lambda q=q, s=s: triton_ops.dequantize_fp8(q, s) for q, s in zip(qr, rs)])

@@ -199,6 +199,17 @@ TFO_API int tfo_fp8_compute_scale_rows(const void* x, int64_t rows, int64_t cols
                                        void* stream);
 TFO_API int tfo_fp8_quantize_rows(const void* x, int64_t rows, int64_t cols, int x_dtype, const float* scales, void* out,
                                   int out_dtype, void* stream);
+/* Per-token dynamic quantize in one launch (extension): for a contiguous
+ * [rows, cols] x, scales_out[r] (x's dtype) = the value
+ * FP8Format.compute_scale_per_channel(x, dim=-1) returns for row r
+ * (triton_ops/models.py:301-314: 448 / max|x[r, :]|, a zero max counting as
+ * 1, rounded in x's dtype), and out = the codes quantize_fp8(x, scales)
+ * produces with those per-row scales (triton_ops/kernels/fp8_quantize.py:
+ * 128-173 with a per-row scale): the bytes of tfo_fp8_compute_scale_rows
+ * followed by tfo_fp8_quantize_rows, from one read of x. out_dtype: U8 or
+ * E4M3. */
+TFO_API int tfo_fp8_quantize_per_token(const void* x, int64_t rows, int64_t cols, int x_dtype, void* scales_out,
+                                       void* out, int out_dtype, void* stream);
 TFO_API int tfo_fp8_dequantize_rows(const void* q, int64_t rows, int64_t cols, int q_dtype, const float* scales,
                                     void* out, int out_dtype, void* stream);
 TFO_API size_t tfo_fp8_gemm_scaled_workspace_bytes(int64_t M, int64_t N, int64_t K, int ab_dtype, int b_layout);

@@ -36,6 +36,41 @@ def test_compute_scale_per_channel_native_equals_reference_expression(cuda, dtyp
     assert torch.equal(FP8Format.compute_scale_per_channel(x, dim=0), torch_per_channel(x, 0))  # torch path
 
 
+@pytest.mark.parametrize("dtype", [torch.float16, torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("code", [torch.uint8, torch.float8_e4m3fn])
+@pytest.mark.parametrize("shape", [(4096, 4096), (2, 3, 256), (37, 100), (5, 8)])
+def test_quantize_per_token_equals_scale_then_quantize(cuda, dtype, code, shape):
+    """One launch gives the bytes of compute_scale_per_channel(x, -1) followed by quantize_fp8(x, scales):
+    the same [..., 1] scales in x's dtype (the reference's torch expression) and the same codes. Rows of
+    whole 16-byte vectors (4096, 256 columns) and element-wise rows (100, 8 columns); a zero row gets 448."""
+    from triton_ops import FP8Format, quantize_fp8, quantize_fp8_per_token
+
+    torch.manual_seed(sum(shape))
+    x = (torch.randn(*shape, device="cuda") * torch.rand(*shape[:-1], 1, device="cuda") * 50).to(dtype)
+    x.view(-1, shape[-1])[1] = 0
+    q, s = quantize_fp8_per_token(x, dtype=code)
+    s_ref = FP8Format.compute_scale_per_channel(x, dim=-1)
+    q_ref, _ = quantize_fp8(x, s_ref, dtype=code)
+    assert s.dtype == s_ref.dtype == dtype and s.shape == s_ref.shape == (*shape[:-1], 1)
+    assert torch.equal(s, s_ref) and torch.equal(s, torch_per_channel(x, -1))
+    assert torch.equal(q.view(torch.uint8), q_ref.view(torch.uint8))
+    if code == torch.uint8:
+        np.testing.assert_array_equal(q.cpu().numpy(), O.quantize_ref(host(x), host(s)))
+
+
+def test_quantize_per_token_one_launch(cuda):
+    """[4096, 4096] fp16: one kernel launch (the two-call form takes three)."""
+    from triton_ops import _lib, quantize_fp8_per_token
+
+    x = torch.randn(4096, 4096, device="cuda").half()
+    quantize_fp8_per_token(x)
+    torch.cuda.synchronize()
+    n0 = _lib.kernel_launches()
+    quantize_fp8_per_token(x)
+    assert _lib.kernel_launches() - n0 == 1
+    assert _lib.device_error_flags() == 0
+
+
 @pytest.mark.parametrize("dt", ["f16", "bf16", "f32"])
 def test_quantize_dequantize_per_row(cuda, dt):
     from triton_ops import FP8Format, dequantize_fp8, quantize_fp8

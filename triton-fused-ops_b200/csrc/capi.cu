@@ -501,6 +501,19 @@ int tfo_fp8_quantize_rows(const void* x, int64_t rows, int64_t cols, int x_dtype
   return e == cudaSuccess ? TFO_OK : cuda_fail(e, fn);
 }
 
+int tfo_fp8_quantize_per_token(const void* x, int64_t rows, int64_t cols, int x_dtype, void* scales_out, void* out,
+                               int out_dtype, void* stream) {
+  const char* fn = "tfo_fp8_quantize_per_token";
+  if (!is_float_dtype(x_dtype)) return fail(TFO_ERR_DTYPE, std::string(fn) + ": x must be f16, bf16 or f32");
+  if (out_dtype != U8 && out_dtype != E4M3) return fail(TFO_ERR_DTYPE, std::string(fn) + ": out must be U8 or E4M3");
+  if (rows < 0 || cols <= 0) return fail(TFO_ERR_INVALID, std::string(fn) + ": bad shape");
+  if (rows == 0) return TFO_OK;
+  if (!x || !scales_out || !out) return fail(TFO_ERR_INVALID, std::string(fn) + ": NULL pointer");
+  const cudaError_t e = quantize_rows_dynamic_launch(x, rows, cols, x_dtype, scales_out, out, out_dtype,
+                                                     static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? TFO_OK : cuda_fail(e, fn);
+}
+
 int tfo_fp8_dequantize_rows(const void* q, int64_t rows, int64_t cols, int q_dtype, const float* scales, void* out,
                             int out_dtype, void* stream) {
   const char* fn = "tfo_fp8_dequantize_rows";

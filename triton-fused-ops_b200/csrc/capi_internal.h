@@ -139,6 +139,9 @@ cudaError_t dequantize_launch(const void* q, int64_t n, int q_dtype, const float
                               cudaStream_t st);
 // Per-row (per-token / per-channel) scales of a [rows, cols] matrix.
 cudaError_t row_scales_launch(const void* x, int64_t rows, int64_t cols, int x_dtype, float* scales, cudaStream_t st);
+// Per-token dynamic quantize in one launch: scales_out[r] (x's dtype) and the codes of row r.
+cudaError_t quantize_rows_dynamic_launch(const void* x, int64_t rows, int64_t cols, int x_dtype, void* scales_out,
+                                         void* out, int out_dtype, cudaStream_t st);
 cudaError_t encode_rows_launch(const void* x, int64_t rows, int64_t cols, int x_dtype, const float* scales, void* out,
                                int out_dtype, cudaStream_t st);
 cudaError_t decode_rows_launch(const void* q, int64_t rows, int64_t cols, int q_dtype, const float* scales, void* out,

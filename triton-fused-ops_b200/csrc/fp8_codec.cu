@@ -467,6 +467,89 @@ __global__ void __launch_bounds__(kRowThreads) encode_rows_kernel(const T* __res
     out[i] = static_cast<uint8_t>(enc1(__fmul_rn(Ty<T>::to_f(x[i]), __ldg(scales + i / cols))));
 }
 
+// ---- per-token dynamic quantize: row scales and codes in one launch --------
+// One warp per row: max |x| over the row (the element-wise fp32 maxima of
+// row_scales_kernel), the row's scale with row_scales_kernel's rounding,
+// written in x's dtype (the value compute_scale_per_channel returns), then
+// the row read again (an L2 hit: this warp has just read it) and encoded with
+// that scale exactly as encode_rows_kernel does. One HBM read of x instead of
+// two, and one launch instead of three (row scales, the cast of the scales to
+// x's dtype, the encode).
+template <typename T, bool E4M3>
+__device__ __forceinline__ uint4 encode_chunk_scaled(const Chunk<T>& c, float s) {
+  float f[16];
+  c.to_f(f);
+  uint32_t w[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    if constexpr (E4M3) {
+      const uint32_t lo = __nv_cvt_float2_to_fp8x2(make_float2(__fmul_rn(f[4 * q], s), __fmul_rn(f[4 * q + 1], s)),
+                                                   __NV_SATFINITE, __NV_E4M3);
+      const uint32_t hi = __nv_cvt_float2_to_fp8x2(
+          make_float2(__fmul_rn(f[4 * q + 2], s), __fmul_rn(f[4 * q + 3], s)), __NV_SATFINITE, __NV_E4M3);
+      w[q] = lo | (hi << 16);
+    } else {
+      w[q] = ref_encode(__fmul_rn(f[4 * q], s)) | (ref_encode(__fmul_rn(f[4 * q + 1], s)) << 8) |
+             (ref_encode(__fmul_rn(f[4 * q + 2], s)) << 16) | (ref_encode(__fmul_rn(f[4 * q + 3], s)) << 24);
+    }
+  }
+  return make_uint4(w[0], w[1], w[2], w[3]);
+}
+
+template <typename T, bool E4M3>
+__global__ void __launch_bounds__(kRowThreads) quantize_rows_dynamic_kernel(const T* __restrict__ x, int64_t rows,
+                                                                            int64_t cols, bool vec,
+                                                                            T* __restrict__ scales_out,
+                                                                            uint8_t* __restrict__ out) {
+  griddep_launch_dependents();  // a programmatic-dependent GEMM that follows may be scheduled early
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = (static_cast<int64_t>(blockIdx.x) * kRowThreads + threadIdx.x) >> 5; r < rows;
+       r += (static_cast<int64_t>(gridDim.x) * kRowThreads) >> 5) {
+    const T* xr = x + r * cols;
+    uint8_t* orow = out + r * cols;
+    uint32_t m = 0;
+    const int64_t cpr = cols / 16;
+    if (vec) {  // rows of whole 16-element chunks, 16-byte aligned: two chunks in flight per lane
+      for (int64_t c = lane; c < cpr; c += 64) {
+        Chunk<T> a, b;
+        a.template load<false>(xr + c * 16);
+        if (c + 32 < cpr) b.template load<false>(xr + (c + 32) * 16);
+        else b.zero();
+        float f[16];
+        a.to_f(f);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) m = max(m, __float_as_uint(fabsf(f[j])));
+        b.to_f(f);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) m = max(m, __float_as_uint(fabsf(f[j])));
+      }
+    } else {
+      for (int64_t c = lane; c < cols; c += 32) m = max(m, __float_as_uint(fabsf(Ty<T>::to_f(xr[c]))));
+    }
+    m = warp_max_u32(m);
+    const float amax = __uint_as_float(m);
+    const float rcp = Ty<T>::to_f(Ty<T>::from_f(__frcp_rn(amax == 0.f ? 1.0f : amax)));
+    const float s = Ty<T>::to_f(Ty<T>::from_f(__fmul_rn(rcp, 448.0f)));
+    if (lane == 0) scales_out[r] = Ty<T>::from_f(s);
+    if (vec) {
+      for (int64_t c = lane; c < cpr; c += 64) {
+        Chunk<T> a, b;
+        const bool has_b = c + 32 < cpr;
+        a.template load<false>(xr + c * 16);
+        if (has_b) b.template load<false>(xr + (c + 32) * 16);
+        __stcs(reinterpret_cast<uint4*>(orow) + c, encode_chunk_scaled<T, E4M3>(a, s));
+        if (has_b) __stcs(reinterpret_cast<uint4*>(orow) + c + 32, encode_chunk_scaled<T, E4M3>(b, s));
+      }
+    } else {
+      for (int64_t c = lane; c < cols; c += 32) {
+        const float v = __fmul_rn(Ty<T>::to_f(xr[c]), s);
+        orow[c] = static_cast<uint8_t>(
+            E4M3 ? static_cast<uint32_t>(__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3)) : ref_encode(v));
+      }
+    }
+  }
+}
+
 // out[r, c] = dec(q[r, c]) / scales[r], dec as in the per-tensor decode.
 // VEC: q and out 16-byte aligned and cols a multiple of 16, so each thread
 // takes one 16-code vector (one row, one scale) and stores its outputs as
@@ -898,6 +981,30 @@ cudaError_t encode_rows_launch(const void* x, int64_t rows, int64_t cols, int x_
     case F16: return enc_rows_t<__half>(x, rows, cols, scales, out, e4, st);
     case BF16: return enc_rows_t<__nv_bfloat16>(x, rows, cols, scales, out, e4, st);
     default: return enc_rows_t<float>(x, rows, cols, scales, out, e4, st);
+  }
+}
+
+template <typename T>
+static cudaError_t quant_rows_dyn_t(const void* x, int64_t rows, int64_t cols, void* scales_out, void* out, bool e4m3,
+                                    cudaStream_t st) {
+  const bool vec = al16(x) && al16(out) && cols % 16 == 0;
+  const int grid = rows_grid(rows * 32);
+  auto* xs = static_cast<const T*>(x);
+  auto* so = static_cast<T*>(scales_out);
+  auto* o = static_cast<uint8_t*>(out);
+  if (e4m3) quantize_rows_dynamic_kernel<T, true><<<grid, kRowThreads, 0, st>>>(xs, rows, cols, vec, so, o);
+  else quantize_rows_dynamic_kernel<T, false><<<grid, kRowThreads, 0, st>>>(xs, rows, cols, vec, so, o);
+  note_launch();
+  return cudaGetLastError();
+}
+
+cudaError_t quantize_rows_dynamic_launch(const void* x, int64_t rows, int64_t cols, int x_dtype, void* scales_out,
+                                         void* out, int out_dtype, cudaStream_t st) {
+  const bool e4 = out_dtype == E4M3;
+  switch (x_dtype) {
+    case F16: return quant_rows_dyn_t<__half>(x, rows, cols, scales_out, out, e4, st);
+    case BF16: return quant_rows_dyn_t<__nv_bfloat16>(x, rows, cols, scales_out, out, e4, st);
+    default: return quant_rows_dyn_t<float>(x, rows, cols, scales_out, out, e4, st);
   }
 }
 

@@ -38,7 +38,7 @@ from triton_ops.exceptions import (
     UnsupportedDtypeError,
 )
 from triton_ops.kernels.fp8_gemm import FP8Linear, fp8_gemm
-from triton_ops.kernels.fp8_quantize import dequantize_fp8, quantize_fp8
+from triton_ops.kernels.fp8_quantize import dequantize_fp8, quantize_fp8, quantize_fp8_per_token
 from triton_ops.kernels.gated_mlp import FusedGatedMLP, fused_gated_mlp, fused_gated_mlp_quantize
 from triton_ops.kernels.rmsnorm_rope import FusedRMSNormRoPE, fused_rmsnorm_rope, fused_rmsnorm_rope_quantize
 from triton_ops.models import (
@@ -61,6 +61,7 @@ __all__ = [
     "fp8_gemm",
     "FP8Linear",
     "quantize_fp8",
+    "quantize_fp8_per_token",
     "dequantize_fp8",
     "TensorSpec",
     "RMSNormRoPEInput",

@@ -72,6 +72,7 @@ _SIGNATURES = {
     "tfo_fp8_dequantize": (_c_int, [_c_vp, _c_i64, _c_int, _c_vp, _c_vp, _c_int, _c_vp]),
     "tfo_fp8_compute_scale_rows": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp]),
     "tfo_fp8_quantize_rows": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_int, _c_vp]),
+    "tfo_fp8_quantize_per_token": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_int, _c_vp]),
     "tfo_fp8_dequantize_rows": (_c_int, [_c_vp, _c_i64, _c_i64, _c_int, _c_vp, _c_vp, _c_int, _c_vp]),
     "tfo_fp8_gemm_scaled_workspace_bytes": (_c_size, [_c_i64, _c_i64, _c_i64, _c_int, _c_int]),
     "tfo_fp8_gemm_scaled": (
