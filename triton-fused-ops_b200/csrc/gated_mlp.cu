@@ -56,6 +56,7 @@ struct GatedEpi {
     const float* scale;     // its multiplier
     int e4m3;               // codes are e4m3 (else the reference codec)
     uint32_t* amax_parts;   // optional: one max |output| per epilogue warp
+    bool stream_out;        // evict-first output stores (an output far larger than L2, not read back)
   };
   struct State {
     float s;        // code multiplier
@@ -76,7 +77,8 @@ struct GatedEpi {
     float v[16];
 #pragma unroll
     for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[0][i]) * act_fn<ACT>(__uint_as_float(r[1][i]));
-    if (p.out != nullptr) store_row16<TO>(p.out + static_cast<int64_t>(row) * p.ldc + col0, v, valid, p.vec_ok);
+    if (p.out != nullptr)
+      store_row16<TO>(p.out + static_cast<int64_t>(row) * p.ldc + col0, v, valid, p.vec_ok, p.stream_out);
     if (p.codes == nullptr && p.amax_parts == nullptr) return;
     // the values the TO output holds
 #pragma unroll
@@ -154,6 +156,7 @@ namespace {
 constexpr int kStages = 4;      // 48 KB stages (one CTA per MMA)
 constexpr int kStagesPair = 6;  // 32 KB stages (two CTAs per MMA)
 constexpr int kBlockN = 128;
+constexpr int64_t kStreamOutBytes = 64ll << 20;  // half the 126 MB L2
 constexpr int kGroupM = 16;
 
 inline int64_t round_up(int64_t v, int64_t m) { return (v + m - 1) / m * m; }
@@ -200,8 +203,16 @@ cudaError_t launch_umma_cg(const CUtensorMap& tx, const CUtensorMap& tg, const C
   auto kern = umma_gemm_kernel<KIND, kBlockN, 2, STAGES, Epi, false, CG>;
   const int resident = gemm_resident_units(reinterpret_cast<const void*>(kern), gemm_threads(4), L::SMEM_BYTES, CG);
   if (resident <= 0) return cudaErrorInvalidConfiguration;
+  // An output of more than half the L2 is written evict-first: its lines then
+  // drain to HBM while the tensor-bound MLP runs instead of after it (the
+  // prefill step [65536, 11264] fp16: MLP 1360-1369 -> 1391-1403 TFLOP/s, the
+  // RMSNorm+RoPE that follows it 235 -> 232 us, alternating runs on one box).
+  // Smaller outputs (decode sizes) stay in L2 for the projection that reads
+  // them; the rows of a dynamic-scale quantize are re-read by its encode.
+  const bool stream_out = g.amax_parts == nullptr &&
+                          g.M * g.N * static_cast<int64_t>(sizeof(TO)) > kStreamOutBytes;
   typename Epi::Params ep{static_cast<TO*>(g.out), g.N, al16(g.out) && (g.N * sizeof(TO)) % 16 == 0, g.codes,
-                          g.scale, g.e4m3, g.amax_parts};
+                          g.scale, g.e4m3, g.amax_parts, stream_out};
   const int64_t tiles = ((g.M + L::PAIR_M - 1) / L::PAIR_M) * ((g.N + kBlockN - 1) / kBlockN);
   const int units = static_cast<int>(std::min<int64_t>(tiles, resident));
   if (g.ctas_out != nullptr) *g.ctas_out = units * CG;
