@@ -42,12 +42,14 @@ def test_compute_scale_per_channel_native_equals_reference_expression(cuda, dtyp
 def test_quantize_per_token_equals_scale_then_quantize(cuda, dtype, code, shape):
     """One launch gives the bytes of compute_scale_per_channel(x, -1) followed by quantize_fp8(x, scales):
     the same [..., 1] scales in x's dtype (the reference's torch expression) and the same codes. Rows of
-    whole 16-byte vectors (4096, 256 columns) and element-wise rows (100, 8 columns); a zero row gets 448."""
+    whole 16-byte vectors (4096, 256 columns) and element-wise rows (100, 8 columns); a zero row gets 448, a
+    row of 1e-6 an infinite fp16 scale (the clamped encode path; finite rows take the in-range one)."""
     from triton_ops import FP8Format, quantize_fp8, quantize_fp8_per_token
 
     torch.manual_seed(sum(shape))
     x = (torch.randn(*shape, device="cuda") * torch.rand(*shape[:-1], 1, device="cuda") * 50).to(dtype)
     x.view(-1, shape[-1])[1] = 0
+    x.view(-1, shape[-1])[2] = 1e-6
     q, s = quantize_fp8_per_token(x, dtype=code)
     s_ref = FP8Format.compute_scale_per_channel(x, dim=-1)
     q_ref, _ = quantize_fp8(x, s_ref, dtype=code)

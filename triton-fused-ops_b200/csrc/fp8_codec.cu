@@ -496,6 +496,16 @@ __device__ __forceinline__ uint4 encode_chunk_scaled(const Chunk<T>& c, float s)
   return make_uint4(w[0], w[1], w[2], w[3]);
 }
 
+// Reference-codec bytes of a chunk whose every |x * s| stays below 449.76
+// (see quantize_rows_dynamic_kernel): the in-range encode, no clamp.
+template <typename T>
+__device__ __forceinline__ uint4 encode_chunk_in_range(const Chunk<T>& c, float s) {
+  float f[16];
+  c.to_f(f);
+  return make_uint4(ref_encode4_in_range_scaled(f, s), ref_encode4_in_range_scaled(f + 4, s),
+                    ref_encode4_in_range_scaled(f + 8, s), ref_encode4_in_range_scaled(f + 12, s));
+}
+
 template <typename T, bool E4M3>
 __global__ void __launch_bounds__(kRowThreads) quantize_rows_dynamic_kernel(const T* __restrict__ x, int64_t rows,
                                                                             int64_t cols, bool vec,
@@ -531,14 +541,27 @@ __global__ void __launch_bounds__(kRowThreads) quantize_rows_dynamic_kernel(cons
     const float rcp = Ty<T>::to_f(Ty<T>::from_f(__frcp_rn(amax == 0.f ? 1.0f : amax)));
     const float s = Ty<T>::to_f(Ty<T>::from_f(__fmul_rn(rcp, 448.0f)));
     if (lane == 0) scales_out[r] = Ty<T>::from_f(s);
+    // Reference codec, fp16 or fp32 rows: s is 448 / amax within three
+    // roundings (at most 0.25 % high, the fp16 reciprocal possibly subnormal),
+    // so every |x * s| < 448 * 127.5 / 127 and rint(RN(RN(c / 448) * 127))
+    // equals the clamped value's: the unclamped in-range encode gives the same
+    // bytes. Not for bf16 (its two roundings can exceed that margin), nor for
+    // a non-finite amax or scale (the clamp and NaN rules then matter).
+    const bool in_range = !E4M3 && !std::is_same<T, __nv_bfloat16>::value && amax < INFINITY && s > 0.f &&
+                          s < INFINITY;
     if (vec) {
       for (int64_t c = lane; c < cpr; c += 64) {
         Chunk<T> a, b;
         const bool has_b = c + 32 < cpr;
         a.template load<false>(xr + c * 16);
         if (has_b) b.template load<false>(xr + (c + 32) * 16);
-        __stcs(reinterpret_cast<uint4*>(orow) + c, encode_chunk_scaled<T, E4M3>(a, s));
-        if (has_b) __stcs(reinterpret_cast<uint4*>(orow) + c + 32, encode_chunk_scaled<T, E4M3>(b, s));
+        if (in_range) {
+          __stcs(reinterpret_cast<uint4*>(orow) + c, encode_chunk_in_range<T>(a, s));
+          if (has_b) __stcs(reinterpret_cast<uint4*>(orow) + c + 32, encode_chunk_in_range<T>(b, s));
+        } else {
+          __stcs(reinterpret_cast<uint4*>(orow) + c, encode_chunk_scaled<T, E4M3>(a, s));
+          if (has_b) __stcs(reinterpret_cast<uint4*>(orow) + c + 32, encode_chunk_scaled<T, E4M3>(b, s));
+        }
       }
     } else {
       for (int64_t c = lane; c < cols; c += 32) {
