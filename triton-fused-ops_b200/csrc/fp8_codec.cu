@@ -541,14 +541,14 @@ __global__ void __launch_bounds__(kRowThreads) quantize_rows_dynamic_kernel(cons
     const float rcp = Ty<T>::to_f(Ty<T>::from_f(__frcp_rn(amax == 0.f ? 1.0f : amax)));
     const float s = Ty<T>::to_f(Ty<T>::from_f(__fmul_rn(rcp, 448.0f)));
     if (lane == 0) scales_out[r] = Ty<T>::from_f(s);
-    // Reference codec, fp16 or fp32 rows: s is 448 / amax within three
-    // roundings (at most 0.25 % high, the fp16 reciprocal possibly subnormal),
-    // so every |x * s| < 448 * 127.5 / 127 and rint(RN(RN(c / 448) * 127))
-    // equals the clamped value's: the unclamped in-range encode gives the same
-    // bytes. Not for bf16 (its two roundings can exceed that margin), nor for
-    // a non-finite amax or scale (the clamp and NaN rules then matter).
-    const bool in_range = !E4M3 && !std::is_same<T, __nv_bfloat16>::value && amax < INFINITY && s > 0.f &&
-                          s < INFINITY;
+    // Reference codec: s is 448 / amax within a few roundings in x's dtype,
+    // so RN(amax * s) is close to 448. When it is at most 449, every
+    // |RN(x * s)| <= RN(amax * s) <= 449 < 448 * 127.5 / 127 (RN is monotonic),
+    // so rint(RN(RN(c / 448) * 127)) equals the clamped value's code and the
+    // unclamped in-range encode gives the same bytes. fp16 and fp32 rows always
+    // pass (at most 0.25 % high); bf16 rows whose two roundings push the
+    // product past 449, and non-finite amax or scales, keep the clamped encode.
+    const bool in_range = !E4M3 && amax < INFINITY && s > 0.f && s < INFINITY && __fmul_rn(amax, s) <= 449.0f;
     if (vec) {
       for (int64_t c = lane; c < cpr; c += 64) {
         Chunk<T> a, b;
