@@ -996,6 +996,11 @@ def run_profile_op(args):
             fn = lambda: triton_ops.fused_rmsnorm_rope_quantize(x, w, cos, sin, scale=two)
         else:
             fn = lambda: triton_ops.quantize_fp8(triton_ops.fused_rmsnorm_rope(x, w, cos, sin), two)
+    elif op == "quantize_per_token":
+        # [4096, 4096] fp16 N(0, 1): per-row scales and codes in one launch
+        t = torch.randn(4096, 4096, device=dev, generator=g).half()
+        qd = torch.float8_e4m3fn if args.profile_dtype == "e4m3" else torch.uint8
+        fn = lambda: triton_ops.quantize_fp8_per_token(t, dtype=qd)
     elif op in ("quantize", "dequantize"):
         # [4096, 4096] fp16 N(0, 1) with 0.1% of entries set to +-200
         t = torch.randn(4096, 4096, device=dev, generator=g).half()
@@ -1023,7 +1028,8 @@ def main():
     ap.add_argument("--no-components", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--profile-op", default=None,
-                    help="run one op --steps times for an ncu capture: gated_mlp, rmsnorm_rope, fp8_gemm, quantize, dequantize")
+                    help="run one op --steps times for an ncu capture: gated_mlp, rmsnorm_rope, fp8_gemm, quantize, "
+                         "dequantize, quantize_per_token")
     ap.add_argument("--profile-shape", default="small", help="small | config1 | config3 | config4 | prefill")
     ap.add_argument("--profile-dtype", default="u8", choices=["u8", "e4m3"],
                     help="8-bit code of the fp8_gemm / quantize / dequantize profile runs")
